@@ -1,0 +1,444 @@
+#!/usr/bin/env python
+"""Benchmark of the ntops LLM operator hot path on B200.
+
+Headline (one JSON line on rank 0): the Llama-3-8B decoder-layer op chain (
+bf16, x [16, 2048, 4096], random-init weights ~N(0, 0.02), synthetic data) in tokens/s,
+whole-job over N GPUs.  The 16 sequences are sharded over the ranks (strong scaling: the
+global batch stays 16 at every N), one process per GPU, no collective on the data path; NCCL is
+used only for barriers and the max-over-ranks timing reduction.
+
+Measured quantities:
+  value      tokens/s with inputs resident in HBM, timed with CUDA events over K steps;
+  e2e        the same through the public API with the step's input copied from pinned host
+             memory and its output copied back inside the timed region;
+  roofline   the GEMM kernel (dominant by FLOPs): algorithmic 2*M*N*K FLOPs per step over the
+             summed CUDA-event time of the GEMM launches, against the measured sustained bf16
+             peak (MEASURED_PEAKS.json);
+  ops        (N = 1) each BASELINE per-op configuration timed alone: GB/s or TFLOP/s and the
+             fraction of the measured HBM copy / burst bf16 peak;
+  cpu_baseline (N = 1, rank 0) PyTorch's CPU implementation of the same chain on a bounded
+             sample (one sequence prefix), all host threads.
+
+``--impl reference`` times the reference side of the comparison: the reference's kernels need
+``ninetoothed`` (not installable here), so the arm runs the chain on PyTorch's CPU operators —
+the oracle the reference's tests use — on the host cores, same metric and config.
+"""
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+METRIC = "Llama-8B layer-chain tokens/s"
+UNIT = "tokens/s"
+GLOBAL_BATCH = 16
+SEQ = 2048
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured (MEASURED_PEAKS.json)"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback (profiling recipe)"
+
+
+def config(world):
+    return {
+        "workload": "llama3_8b_layer_chain (BASELINE config 3): rms_norm, q/k/v mm, rope, causal GQA sdpa, "
+        "o mm, residual add, rms_norm, gate/up mm, silu*mul, down mm",
+        "global_batch": GLOBAL_BATCH,
+        "seq_len": SEQ,
+        "parallelism": f"dp{world} (sequences sharded, no data-path collective)",
+        "l2": "inputs larger than L2 (x 268 MB + weights 436 MB per pass)",
+    }
+
+
+# ------------------------------------------------------------------------- clocks ---------
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML every 100 ms (read-only)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+# ---------------------------------------------------------------------- CPU chain ---------
+def cpu_chain_sample(tokens, threads=None):
+    """Times PyTorch's CPU implementation of the chain on one sequence prefix of `tokens`."""
+    from oracle.chain import layer_forward_torch_cpu
+    from ntops_b200.chain import FFN, HEAD_DIM, HEADS, HIDDEN, KV_HEADS, THETA
+
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    dt = torch.bfloat16
+
+    def w(k, n):
+        return (torch.randn((k, n), generator=g) * 0.02).to(dt)
+
+    wts = [w(HIDDEN, HEADS * HEAD_DIM), w(HIDDEN, KV_HEADS * HEAD_DIM), w(HIDDEN, KV_HEADS * HEAD_DIM),
+           w(HEADS * HEAD_DIM, HIDDEN), w(HIDDEN, FFN), w(HIDDEN, FFN), w(FFN, HIDDEN),
+           torch.ones(HIDDEN, dtype=dt), torch.ones(HIDDEN, dtype=dt)]
+    inv = THETA ** (-2 * (torch.arange(HEAD_DIM // 2, dtype=torch.float64) / HEAD_DIM))
+    pos = torch.arange(tokens, dtype=torch.float64)[:, None]
+    sin, cos = torch.sin(pos * inv).to(dt), torch.cos(pos * inv).to(dt)
+    x = torch.randn((1, tokens, HIDDEN), generator=g).to(dt)
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        y = layer_forward_torch_cpu(x, wts, sin, cos)
+        dt_s = time.perf_counter() - t0
+    assert torch.isfinite(y.float()).all()
+    return dt_s, threads
+
+
+def pick_cpu_tokens(target_s=4.0):
+    """Largest power-of-two sequence prefix (128..2048) whose CPU pass stays near target_s."""
+    t128, _ = cpu_chain_sample(128)
+    tokens = 128
+    while tokens < SEQ and t128 * (tokens * 2 / 128) * 1.2 < target_s:
+        tokens *= 2
+    return tokens
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    tokens = pick_cpu_tokens()
+    for _ in range(args.warmup):
+        cpu_chain_sample(tokens)
+    times = []
+    threads = os.cpu_count()
+    for _ in range(args.steps):
+        t, threads = cpu_chain_sample(tokens)
+        times.append(t)
+    total = sum(times)
+    value = tokens * args.steps / total
+    sample = f"1 sequence x {tokens} tokens per step (prefix of a {SEQ}-token sequence), bf16, torch CPU ops"
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(world),
+        "impl": "reference",
+        "reference_note": "reference kernels need ninetoothed (not installed, no network): the arm runs "
+        "PyTorch's CPU operators, the oracle of the reference's own tests",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------- per-op table ------
+def time_op(fn, iters=10, warmup=3, flush=None):
+    """Median CUDA-event time (ms) of fn(); `flush` (writing > L2) runs between iterations."""
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times)
+
+
+def per_op_table(dev, peaks):
+    import ntops_b200.torch as nt
+
+    flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def flush():
+        flush_buf.fill_(1)
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    n = 1 << 28
+    res = {}
+
+    def bw(name, fn, nbytes, use_flush=False):
+        ms = time_op(fn, flush=flush if use_flush else None)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 3)}
+
+    def tf(name, fn, flops):
+        ms = time_op(fn, iters=5, warmup=2)
+        t = flops / (ms * 1e-3) / 1e12
+        res[name] = {"ms": round(ms, 3), "TFLOP/s": round(t, 1), "frac": round(t / peaks["bf16_tflops"], 3)}
+
+    for dt, tag in ((torch.float32, "f32"), (torch.float16, "f16"), (torch.bfloat16, "bf16")):
+        es = torch.tensor([], dtype=dt).element_size()
+        a = (torch.rand(n, generator=g, device=dev) * 8 - 4).to(dt)
+        b = (torch.rand(n, generator=g, device=dev) * 8 - 4).to(dt)
+        e = (torch.rand(n, generator=g, device=dev) * 1.5 + 0.5).to(dt)
+        for name, fn in (("add", lambda: nt.add(a, b)), ("mul", lambda: nt.mul(a, b)), ("div", lambda: nt.div(a, b)),
+                         ("pow", lambda: nt.pow(a, e))):
+            bw(f"{name}_{tag}", fn, 3 * n * es)
+        for name, fn in (("silu", lambda: nt.silu(a)), ("gelu_tanh", lambda: nt.gelu(a, approximate="tanh")),
+                         ("sigmoid", lambda: nt.sigmoid(a)), ("exp", lambda: nt.exp(a)),
+                         ("clamp", lambda: nt.clamp(a, -1, 1))):
+            bw(f"{name}_{tag}", fn, 2 * n * es)
+        del a, b, e
+    ah = torch.randn(n, generator=g, device=dev).to(torch.float16)
+    bh = torch.randn(n, generator=g, device=dev).to(torch.float16)
+    bw("eq_f16", lambda: nt.eq(ah, bh), n * 5)
+    bw("lt_f16", lambda: nt.lt(ah, bh), n * 5)
+    del ah, bh
+    ia = torch.randint(-2**31, 2**31 - 1, (n,), generator=g, device=dev, dtype=torch.int32)
+    ib = torch.randint(-2**31, 2**31 - 1, (n,), generator=g, device=dev, dtype=torch.int32)
+    bw("bitwise_and_i32", lambda: nt.bitwise_and(ia, ib), 3 * n * 4)
+    bw("bitwise_or_i32", lambda: nt.bitwise_or(ia, ib), 3 * n * 4)
+    bw("bitwise_not_i32", lambda: nt.bitwise_not(ia), 2 * n * 4)
+    del ia, ib
+    c1 = torch.randn(4096, 1, generator=g, device=dev)
+    r1 = torch.randn(1, 65536, generator=g, device=dev)
+    bw("broadcast_add_f32", lambda: nt.add(c1, r1), 4096 * 65536 * 4 + (4096 + 65536) * 4)
+    # C1 rms_norm (134 MB: below L2, so L2 is flushed between iterations)
+    x1 = torch.randn(8, 512, 4096, generator=g, device=dev)
+    w1 = 1 + 0.1 * torch.randn(4096, generator=g, device=dev)
+    bw("rms_norm_f32_8x512x4096", lambda: nt.rms_norm(x1, (4096,), w1, 1e-6), 2 * x1.numel() * 4 + 4096 * 4,
+       use_flush=True)
+    del x1
+    # C4
+    xs = torch.randn(4096, 32768, generator=g, device=dev) * 2
+    bw("softmax_f32_4096x32768", lambda: nt.softmax(xs, -1), 2 * xs.numel() * 4)
+    del xs
+    xl = torch.randn(32768, 8192, generator=g, device=dev).to(torch.bfloat16)
+    wl = (1 + 0.1 * torch.randn(8192, generator=g, device=dev)).to(torch.bfloat16)
+    bl = (0.1 * torch.randn(8192, generator=g, device=dev)).to(torch.bfloat16)
+    bw("layer_norm_bf16_32768x8192", lambda: nt.layer_norm(xl, (8192,), wl, bl, 1e-5), 2 * xl.numel() * 2 + 4 * 8192)
+    del xl
+    # RoPE at the chain's q / k sizes
+    from ntops_b200.chain import rope_tables
+
+    q = torch.randn(16, 2048, 32, 128, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(16, 2048, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    sn, cs = rope_tables(2048, dev)
+    bw("rope_bf16_q", lambda: nt.rotary_position_embedding(q, sn, cs, interleaved=False), 2 * q.numel() * 2)
+    bw("rope_bf16_k", lambda: nt.rotary_position_embedding(k, sn, cs, interleaved=False), 2 * k.numel() * 2)
+    del q, k
+    # C5
+    A = (torch.randn(16384, 8192, generator=g, device=dev)).to(torch.bfloat16)
+    B = (torch.randn(8192, 8192, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    bias = torch.randn(8192, generator=g, device=dev).to(torch.bfloat16)
+    tf("addmm_bf16_16384x8192x8192", lambda: nt.addmm(bias, A, B), 2 * 16384 * 8192 * 8192)
+    del A, B
+    qa = torch.randn(8, 32, 8192, 128, generator=g, device=dev).to(torch.bfloat16)
+    ka = torch.randn(8, 32, 8192, 128, generator=g, device=dev).to(torch.bfloat16)
+    va = torch.randn(8, 32, 8192, 128, generator=g, device=dev).to(torch.bfloat16)
+    fl = 4 * 8 * 32 * 8192 * 8192 * 128
+    tf("sdpa_bf16_8x32x8192x128", lambda: nt.scaled_dot_product_attention(qa, ka, va), fl)
+    tf("sdpa_causal_bf16_8x32x8192x128", lambda: nt.scaled_dot_product_attention(qa, ka, va, is_causal=True),
+       fl * (8192 + 1) / (2 * 8192))
+    return res
+
+
+# ---------------------------------------------------------------------------- main --------
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ntops_b200", choices=["ntops_b200", "reference"])
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-op table")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch.distributed as dist
+
+    import ntops_b200.torch as nt  # noqa: F401
+    from ntops_b200 import _lib, chain
+    from ntops_b200.shard import max_over_ranks, shard_range
+    from ntops_b200.torch import utils as ntu
+
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    peaks, peak_src = load_peaks()
+
+    s0, s1 = shard_range(GLOBAL_BATCH, rank, world)
+    batch = s1 - s0
+    tokens = batch * SEQ
+    wts = chain.LayerWeights(dev)
+    sin, cos = chain.rope_tables(SEQ, dev)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn((batch, SEQ, chain.HIDDEN), generator=g, device=dev).to(torch.bfloat16)
+    mm_flops, attn_flops = chain.layer_flops(batch, SEQ)
+
+    for _ in range(args.warmup):
+        chain.layer_forward(x, wts, sin, cos)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    gemm_events = []
+
+    def mm_hook(fn, a, b):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = fn(a, b)
+        e.record()
+        gemm_events.append((s, e))
+        return out
+
+    # ---- timed region: inputs resident in HBM
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ntu.launch_count
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            y = chain.layer_forward(x, wts, sin, cos, mm_hook=mm_hook)
+        end.record()
+        torch.cuda.synchronize()
+    launches = ntu.launch_count - launches0
+    ms_local = start.elapsed_time(end)
+    gemm_ms = sum(s.elapsed_time(e) for s, e in gemm_events)
+    ms = max_over_ranks(ms_local, dev)
+    value = GLOBAL_BATCH * SEQ * args.steps / (ms * 1e-3)
+    gemm_tflops = mm_flops * args.steps / (gemm_ms * 1e-3) / 1e12
+    rc = _lib.load().ntb_check_device_error(None)
+    assert rc == 0, "a kernel reported a device-side timeout"
+    checksum = float(y.float().abs().mean())
+    assert checksum == checksum and checksum > 0, "non-finite layer output"
+
+    # ---- end to end: pinned host input in, output back, every step
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+    xd = torch.empty_like(x)
+    for _ in range(2):
+        xd.copy_(xh, non_blocking=True)
+        yh.copy_(chain.layer_forward(xd, wts, sin, cos), non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        xd.copy_(xh, non_blocking=True)
+        yh.copy_(chain.layer_forward(xd, wts, sin, cos), non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(s2.elapsed_time(e2), dev)
+    e2e_value = GLOBAL_BATCH * SEQ * args.steps / (ms_e2e * 1e-3)
+
+    ops = None
+    cpu = None
+    if world == 1 and rank == 0:
+        if not args.no_ops:
+            del xd
+            ops = per_op_table(dev, peaks)
+        if not args.no_cpu:
+            ctoks = pick_cpu_tokens()
+            t, threads = cpu_chain_sample(ctoks)
+            cpu = {"value": ctoks / t, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"1 sequence x {ctoks} tokens (prefix of a {SEQ}-token sequence), bf16, "
+                   "PyTorch CPU operators"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded randn inputs, random-init weights ~N(0,0.02))",
+            "config": config(world),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": x.numel() * 2 * world,
+                    "d2h_bytes_per_step": y.numel() * 2 * world},
+            "gpu_launches": launches * world,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, 7 projections per step)",
+                         "achieved": gemm_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                         "frac": gemm_tflops / peaks["bf16_tflops_sustained"], "traffic": None,
+                         "peak_source": f"bf16_tflops_sustained, {peak_src}",
+                         "gemm_share_of_step": gemm_ms / ms_local},
+            "step_tflops": (mm_flops + attn_flops) * GLOBAL_BATCH / batch / (ms / args.steps * 1e-3) / 1e12,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+            "ops": ops,
+            "peaks": {k: v for k, v in peaks.items()},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,217 @@
+// Per-element operator functors.  Each computes in opmath (fp32 for half/bf16, fp64 for
+// double, the integer type itself for integers) and follows the CUDA semantics that PyTorch
+// gives the same operator, which is the oracle the reference's tests compare against
+// (tests/test_<op>.py in the ntops project).  Transcendentals call CUDA's accurate math
+// functions (expf, erff, tanhf, powf, sinf, cosf, sqrtf), never the __ intrinsics.
+#pragma once
+
+#include <math.h>
+
+#include "ntb_common.cuh"
+
+namespace ntb {
+namespace ops {
+
+template <typename T> __device__ __forceinline__ bool is_nan(T x) { return x != x; }
+__device__ __forceinline__ float m_exp(float x) { return expf(x); }
+__device__ __forceinline__ double m_exp(double x) { return exp(x); }
+__device__ __forceinline__ float m_erf(float x) { return erff(x); }
+__device__ __forceinline__ double m_erf(double x) { return erf(x); }
+__device__ __forceinline__ float m_tanh(float x) { return tanhf(x); }
+__device__ __forceinline__ double m_tanh(double x) { return tanh(x); }
+__device__ __forceinline__ float m_sqrt(float x) { return sqrtf(x); }
+__device__ __forceinline__ double m_sqrt(double x) { return sqrt(x); }
+__device__ __forceinline__ float m_sin(float x) { return sinf(x); }
+__device__ __forceinline__ double m_sin(double x) { return sin(x); }
+__device__ __forceinline__ float m_cos(float x) { return cosf(x); }
+__device__ __forceinline__ double m_cos(double x) { return cos(x); }
+__device__ __forceinline__ float m_pow(float a, float b) { return powf(a, b); }
+__device__ __forceinline__ double m_pow(double a, double b) { return pow(a, b); }
+__device__ __forceinline__ float m_fmod(float a, float b) { return fmodf(a, b); }
+__device__ __forceinline__ double m_fmod(double a, double b) { return fmod(a, b); }
+__device__ __forceinline__ float m_floor(float a) { return floorf(a); }
+__device__ __forceinline__ double m_floor(double a) { return floor(a); }
+__device__ __forceinline__ float m_trunc(float a) { return truncf(a); }
+__device__ __forceinline__ double m_trunc(double a) { return trunc(a); }
+__device__ __forceinline__ float m_copysign(float a, float b) { return copysignf(a, b); }
+__device__ __forceinline__ double m_copysign(double a, double b) { return copysign(a, b); }
+__device__ __forceinline__ float m_abs(float a) { return fabsf(a); }
+__device__ __forceinline__ double m_abs(double a) { return fabs(a); }
+
+// ------------------------------------------------------------------------ unary -----------
+struct Copy { template <typename T> __device__ T operator()(T x) const { return x; } };
+struct Neg {
+  template <typename T> __device__ T operator()(T x) const { return -x; }
+  __device__ bool operator()(bool x) const { return x; }
+};
+struct Abs {
+  __device__ float operator()(float x) const { return fabsf(x); }
+  __device__ double operator()(double x) const { return fabs(x); }
+  template <typename T> __device__ T operator()(T x) const { return x < T(0) ? T(-x) : x; }
+  __device__ bool operator()(bool x) const { return x; }
+};
+// relu = clamp_min(x, 0) with NaN propagation.
+struct Relu {
+  template <typename T> __device__ T operator()(T x) const { return (is_nan(x) || x > T(0)) ? x : T(0); }
+  __device__ bool operator()(bool x) const { return x; }
+};
+struct Exp { template <typename T> __device__ T operator()(T x) const { return m_exp(x); } };
+struct Sigmoid {
+  template <typename T> __device__ T operator()(T x) const { return T(1) / (T(1) + m_exp(-x)); }
+};
+struct Silu {
+  template <typename T> __device__ T operator()(T x) const { return x / (T(1) + m_exp(-x)); }
+};
+struct Gelu {
+  template <typename T> __device__ T operator()(T x) const {
+    const T kAlpha = T(0.70710678118654752440);  // 1/sqrt(2)
+    return x * T(0.5) * (T(1) + m_erf(x * kAlpha));
+  }
+};
+struct GeluTanh {
+  template <typename T> __device__ T operator()(T x) const {
+    const T kBeta = T(0.79788456080286535588);  // sqrt(2/pi)
+    const T kKappa = T(0.044715);
+    T inner = kBeta * (x + kKappa * x * x * x);
+    return T(0.5) * x * (T(1) + m_tanh(inner));
+  }
+};
+struct Tanh { template <typename T> __device__ T operator()(T x) const { return m_tanh(x); } };
+struct Rsqrt { template <typename T> __device__ T operator()(T x) const { return T(1) / m_sqrt(x); } };
+struct Sin { template <typename T> __device__ T operator()(T x) const { return m_sin(x); } };
+struct Cos { template <typename T> __device__ T operator()(T x) const { return m_cos(x); } };
+struct IsNan { template <typename T> __device__ bool operator()(T x) const { return is_nan(x); } };
+struct IsInf {
+  __device__ bool operator()(float x) const { return isinf(x); }
+  __device__ bool operator()(double x) const { return isinf(x); }
+  template <typename T> __device__ bool operator()(T) const { return false; }
+};
+struct BitwiseNot {
+  template <typename T> __device__ T operator()(T x) const { return T(~x); }
+  __device__ bool operator()(bool x) const { return !x; }
+};
+// clamp with scalar bounds: NaN propagates; min applied before max (torch.clamp).
+template <typename M>
+struct ClampScalar {
+  M lo, hi;
+  int has_lo, has_hi;
+  __device__ M operator()(M x) const {
+    if (is_nan(x)) return x;
+    if (has_lo) x = x < lo ? lo : x;
+    if (has_hi) x = x > hi ? hi : x;
+    return x;
+  }
+};
+
+// ----------------------------------------------------------------------- binary -----------
+template <typename M>
+struct Add {
+  M alpha;
+  __device__ M operator()(M a, M b) const { return a + alpha * b; }
+};
+template <>
+struct Add<bool> {
+  bool alpha;
+  __device__ bool operator()(bool a, bool b) const { return a || (alpha && b); }
+};
+template <typename M>
+struct Sub {
+  M alpha;
+  __device__ M operator()(M a, M b) const { return a - alpha * b; }
+};
+struct Mul {
+  template <typename T> __device__ T operator()(T a, T b) const { return a * b; }
+  __device__ bool operator()(bool a, bool b) const { return a && b; }
+};
+struct Div {
+  template <typename T> __device__ T operator()(T a, T b) const { return a / b; }
+};
+struct DivTrunc {
+  __device__ float operator()(float a, float b) const { return truncf(a / b); }
+  __device__ double operator()(double a, double b) const { return trunc(a / b); }
+  template <typename T> __device__ T operator()(T a, T b) const { return b == T(0) ? T(0) : T(a / b); }
+};
+// Floor division for floating point: the algorithm of CPython's float floor division
+// (Objects/floatobject.c, float_divmod), which is also what torch uses:
+// compute the remainder with fmod, correct its sign towards the divisor, then round the exact
+// quotient (a - mod) / b to the nearest integer from below.
+struct DivFloor {
+  template <typename T>
+  __device__ T flt(T a, T b) const {
+    if (b == T(0)) return a / b;
+    T mod = m_fmod(a, b);
+    T div = (a - mod) / b;
+    if (mod != T(0) && ((b < T(0)) != (mod < T(0)))) div -= T(1);
+    T fd;
+    if (div != T(0)) {
+      fd = m_floor(div);
+      if (div - fd > T(0.5)) fd += T(1);
+    } else {
+      fd = m_copysign(T(0), a / b);
+    }
+    return fd;
+  }
+  __device__ float operator()(float a, float b) const { return flt(a, b); }
+  __device__ double operator()(double a, double b) const { return flt(a, b); }
+  template <typename T> __device__ T operator()(T a, T b) const {
+    if (b == T(0)) return T(0);
+    T q = a / b;
+    if ((a % b != T(0)) && ((a < T(0)) != (b < T(0)))) q -= T(1);
+    return q;
+  }
+};
+struct Pow {
+  __device__ float operator()(float a, float b) const { return m_pow(a, b); }
+  __device__ double operator()(double a, double b) const { return m_pow(a, b); }
+  // Integer power by squaring; negative exponents give 0 except for bases 1 and -1.
+  template <typename T> __device__ T operator()(T base, T e) const {
+    if (e < T(0)) {
+      if (base == T(1)) return T(1);
+      if (base == T(-1)) return (e % T(2) == T(0)) ? T(1) : T(-1);
+      return T(0);
+    }
+    T r = T(1);
+    while (e) {
+      if (e & T(1)) r = T(r * base);
+      base = T(base * base);
+      e = T(e >> 1);
+    }
+    return r;
+  }
+};
+struct Eq { template <typename T> __device__ bool operator()(T a, T b) const { return a == b; } };
+struct Ne { template <typename T> __device__ bool operator()(T a, T b) const { return a != b; } };
+struct Lt { template <typename T> __device__ bool operator()(T a, T b) const { return a < b; } };
+struct Le { template <typename T> __device__ bool operator()(T a, T b) const { return a <= b; } };
+struct Gt { template <typename T> __device__ bool operator()(T a, T b) const { return a > b; } };
+struct Ge { template <typename T> __device__ bool operator()(T a, T b) const { return a >= b; } };
+struct BitAnd {
+  template <typename T> __device__ T operator()(T a, T b) const { return T(a & b); }
+  __device__ bool operator()(bool a, bool b) const { return a && b; }
+};
+struct BitOr {
+  template <typename T> __device__ T operator()(T a, T b) const { return T(a | b); }
+  __device__ bool operator()(bool a, bool b) const { return a || b; }
+};
+
+// ---------------------------------------------------------------------- ternary -----------
+// clamp with tensor bounds (torch semantics: NaN in any operand propagates).  Missing bounds
+// are passed as the input itself so they never bind.
+struct ClampTensor {
+  int has_lo, has_hi;
+  template <typename T> __device__ T operator()(T x, T lo, T hi) const {
+    if (is_nan(x)) return x;
+    if (has_lo) {
+      if (is_nan(lo)) return lo;
+      x = x < lo ? lo : x;
+    }
+    if (has_hi) {
+      if (is_nan(hi)) return hi;
+      x = x > hi ? hi : x;
+    }
+    return x;
+  }
+};
+
+}  // namespace ops
+}  // namespace ntb

@@ -1,0 +1,607 @@
+// ntb_sdpa: scaled dot-product attention.
+//
+// Reference (ntops kernels/scaled_dot_product_attention.py:154-201): per (batch, kv-head,
+// q-block) program, loop over the GQA group's q-heads and over every KV block: S = Q K^T,
+// mask out-of-range keys, add the additive mask, apply the causal mask (upper-left: k <= q,
+// lower-right: k <= q + Skv - Sq), online softmax in base 2, acc = acc * alpha + P V, finally
+// acc / l.  The reference does not skip KV blocks above the causal diagonal.
+//
+// sm_100a kernel (bf16 / fp16, head_dim 64 or 128, no additive mask):
+//   * one CTA per (batch, q-head, 128-row Q tile); heavy causal tiles are launched first;
+//   * warp 4 loads Q once and streams K / V blocks of 128 keys through a 2-deep TMA ring;
+//   * warp 5 owns TMEM (O: D columns, three S buffers of 128 columns) and issues
+//       S_j = Q K_j^T            (A = Q, B = K, both K-major, from shared memory)
+//       O  += P_j V_j            (A = P from TMEM, B = V MN-major from shared memory)
+//     in the order S_0, S_1, PV_0, S_2, PV_1, ... so the tensor core computes S_{j+1} while the
+//     softmax warps work on S_j;
+//   * warps 0-3 (one thread per query row) read S_j from TMEM, mask the diagonal / tail
+//     blocks, track the running max in base-2 units, write P_j = exp2(S*scale*log2e - m) as
+//     bf16/fp16 pairs over S_j's first 64 TMEM columns, and accumulate the row sum.  The O
+//     accumulator is rescaled only when a row's max grows by more than 8 (2^8 headroom), so
+//     O and l always share one reference max and O / l is exact;
+//   * causal KV blocks wholly above the diagonal are skipped.
+// fp32 / fp64 operands, additive masks, other head sizes and layouts TMA cannot address run
+// on the CUDA-core kernel at the end of this file (fp32 accumulation, fp64 for fp64).
+#include <atomic>
+#include <type_traits>
+
+#include "elementwise.cuh"
+#include "sm100.cuh"
+#include "tma.cuh"
+
+namespace ntb {
+namespace fmha {
+
+constexpr int BLK = 128;         // query rows per CTA and keys per KV block
+constexpr int kThreads = 192;    // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;
+
+struct Params {
+  int B, Hq, Hkv, Sq, Skv, D;
+  int group;        // Hq / Hkv
+  int causal;       // 0 none, 1 upper-left, 2 lower-right
+  int nq;           // q tiles per head
+  float scale_log2; // scale * log2(e)
+  void* o;
+  int64_t o_b, o_h, o_s;  // output strides (unit inner stride)
+  unsigned int* err;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int SUB = BLK * 128;              // one [128 rows][128 B] swizzled sub-tile
+  static constexpr int NSUB = D / 64;                // 64-element chunks of head_dim
+  static constexpr int TILE = SUB * NSUB;            // Q, K or V tile
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = TILE;
+  static constexpr int V_OFF = 3 * TILE;
+  static constexpr int BAR_OFF = 5 * TILE;
+  static constexpr int TOTAL = 5 * TILE + 1024 + 256;
+};
+
+__device__ __forceinline__ int num_kv_blocks(const Params& p, int q0) {
+  int nb = (p.Skv + BLK - 1) / BLK;
+  if (p.causal) {
+    const int off = p.causal == 2 ? p.Skv - p.Sq : 0;
+    const int last_key = q0 + BLK - 1 + off;  // largest key any row of the tile may see
+    if (last_key < 0) return 0;
+    nb = min(nb, last_key / BLK + 1);
+  }
+  return nb;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    fmha_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, Params p) {
+  using S = Smem<D>;
+  constexpr uint32_t kFormat = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t O_COL = 0;
+  constexpr uint32_t S_COL0 = 128;  // S buffer b at S_COL0 + 128 * b, b = 0..2
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + S::Q_OFF;
+  uint8_t* sK = smem + S::K_OFF;  // 2 stages
+  uint8_t* sV = smem + S::V_OFF;  // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [3]
+  uint64_t* p_full = bars + 12;   // [3]
+  uint64_t* pv_done = bars + 15;  // [3]: PV_j commits to pv_done[j % 3]
+  uint64_t* done_bar = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh_count = p.B * p.Hq;
+  const int qt = p.nq - 1 - (int)(blockIdx.x / bh_count);  // heavy (late) tiles first
+  const int bh = (int)(blockIdx.x % bh_count);
+  const int b = bh / p.Hq, hq = bh % p.Hq, hkv = hq / p.group;
+  const int q0 = qt * BLK;
+  const int nkv = num_kv_blocks(p, q0);
+
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&k_full[i], 1);
+      sm100::mbar_init(&k_empty[i], 1);
+      sm100::mbar_init(&v_full[i], 1);
+      sm100::mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 3; ++i) {
+      sm100::mbar_init(&s_full[i], 1);
+      sm100::mbar_init(&p_full[i], 128);
+      sm100::mbar_init(&pv_done[i], 1);
+    }
+    sm100::mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  if (warp == 5) {
+    sm100::tmem_alloc(tmem_slot, TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ TMA producer ----
+    if (lane == 0 && nkv > 0) {
+      uint32_t armed_k = 0, armed_v = 0, par_k = 0, par_v = 0;
+      bool ok = true;
+      sm100::mbar_arrive_expect_tx(q_full, S::TILE);
+#pragma unroll
+      for (int c = 0; c < S::NSUB; ++c) sm100::tma_load_4d(sQ + c * S::SUB, &tq, q_full, c * 64, q0, hq, b);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!sm100::mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+        sm100::mbar_arrive_expect_tx(&k_full[st], S::TILE);
+        armed_k |= 1u << st;
+        par_k = (par_k & ~(1u << st)) | (ph << st);
+#pragma unroll
+        for (int c = 0; c < S::NSUB; ++c)
+          sm100::tma_load_4d(sK + st * S::TILE + c * S::SUB, &tk, &k_full[st], c * 64, j * BLK, hkv, b);
+        if (!sm100::mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+        sm100::mbar_arrive_expect_tx(&v_full[st], S::TILE);
+        armed_v |= 1u << st;
+        par_v = (par_v & ~(1u << st)) | (ph << st);
+#pragma unroll
+        for (int c = 0; c < S::NSUB; ++c)
+          sm100::tma_load_4d(sV + st * S::TILE + c * S::SUB, &tv, &v_full[st], c * 64, j * BLK, hkv, b);
+      }
+      sm100::mbar_wait_unwind(q_full, 0);
+      for (int s = 0; s < 2; ++s) {
+        if (armed_k & (1u << s)) sm100::mbar_wait_unwind(&k_full[s], (par_k >> s) & 1u);
+        if (armed_v & (1u << s)) sm100::mbar_wait_unwind(&v_full[s], (par_v >> s) & 1u);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------- MMA issuer ----
+    constexpr uint32_t idesc_qk = sm100::instr_desc(kFormat, false, false, BLK, BLK);
+    constexpr uint32_t idesc_pv = sm100::instr_desc(kFormat, false, true, BLK, D);
+    bool ok = nkv > 0 && sm100::mbar_wait(q_full, 0, abort_flag, p.err);
+    sm100::tc_fence_after();
+    const uint32_t q_addr = sm100::smem_u32(sQ);
+    int issued_s = 0;  // S blocks issued
+    auto issue_s = [&](int j) -> bool {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (j >= 3) {  // S buffer j%3 held P_{j-3}: wait for PV_{j-3} to finish reading it
+        if (!sm100::mbar_wait(&pv_done[j % 3], (uint32_t)(((j - 3) / 3) & 1), abort_flag, p.err)) return false;
+      }
+      if (!sm100::mbar_wait(&k_full[st], ph, abort_flag, p.err)) return false;
+      sm100::tc_fence_after();
+      if (lane == 0) {
+        const uint32_t k_addr = sm100::smem_u32(sK + st * S::TILE);
+        const uint32_t d_tmem = tmem + S_COL0 + 128u * (uint32_t)(j % 3);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * S::SUB + (kk & 3) * 32;
+          sm100::mma_f16(d_tmem, sm100::smem_desc(q_addr + off, 16, 1024),
+                         sm100::smem_desc(k_addr + off, 16, 1024), idesc_qk, kk != 0);
+        }
+        sm100::mma_commit(&k_empty[st]);
+        sm100::mma_commit(&s_full[j % 3]);
+      }
+      __syncwarp();
+      return true;
+    };
+    auto issue_pv = [&](int j) -> bool {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!sm100::mbar_wait(&p_full[j % 3], (uint32_t)((j / 3) & 1), abort_flag, p.err)) return false;
+      if (!sm100::mbar_wait(&v_full[st], ph, abort_flag, p.err)) return false;
+      sm100::tc_fence_after();
+      if (lane == 0) {
+        const uint32_t v_addr = sm100::smem_u32(sV + st * S::TILE);
+        const uint32_t p_tmem = tmem + S_COL0 + 128u * (uint32_t)(j % 3);
+#pragma unroll
+        for (int kk = 0; kk < BLK / 16; ++kk) {
+          sm100::mma_f16_ts(tmem + O_COL, p_tmem + kk * 8,
+                            sm100::smem_desc(v_addr + kk * 16 * 128, S::SUB, 1024), idesc_pv,
+                            (j | kk) != 0);
+        }
+        sm100::mma_commit(&v_empty[st]);
+        sm100::mma_commit(&pv_done[j % 3]);
+      }
+      __syncwarp();
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    if (ok && nkv > 1) ok = issue_s(1);
+    issued_s = nkv > 1 ? 2 : 1;
+    for (int j = 0; ok && j < nkv; ++j) {
+      ok = issue_pv(j);
+      if (ok && issued_s < nkv) {
+        ok = issue_s(issued_s);
+        ++issued_s;
+      }
+    }
+    if (lane == 0) {
+      sm100::mma_commit(done_bar);
+      sm100::mbar_wait_unwind(done_bar, 0);
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------------------------------- softmax warps ----
+    const int row = q0 + warp * 32 + lane;  // warp w reads TMEM lanes 32w..32w+31
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const int off = p.causal == 2 ? p.Skv - p.Sq : 0;
+    float m_used = -INFINITY;  // reference max of P and O (base-2 units)
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!sm100::mbar_wait(&s_full[j % 3], (uint32_t)((j / 3) & 1), abort_flag, p.err)) { ok = false; break; }
+      sm100::tc_fence_after();
+      const uint32_t s_tmem = tmem + S_COL0 + 128u * (uint32_t)(j % 3) + lane_addr;
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, r);
+        sm100::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      const int k0 = j * BLK;
+      const bool need_mask = (k0 + BLK > p.Skv) || (p.causal && k0 + BLK - 1 > q0 + off);
+      if (need_mask) {
+        const int kmax = p.causal ? min(p.Skv - 1, row + off) : p.Skv - 1;
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (k0 + i > kmax) s[i] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      const float m_blk = mx * p.scale_log2;
+      // Rescale O and l only when the max grows by more than the threshold.
+      const bool grow = m_blk > m_used + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, grow && j > 0)) {
+        float alpha = 1.f;
+        if (grow) alpha = exp2f(m_used - m_blk);
+        // PV_{j-1} (and, by commit order, every earlier PV) must have finished writing O.
+        if (!sm100::mbar_wait(&pv_done[(j - 1) % 3], (uint32_t)(((j - 1) / 3) & 1), abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld_32x32b_x32(tmem + O_COL + c * 32 + lane_addr, r);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          sm100::tmem_st_32x32b_x32(tmem + O_COL + c * 32 + lane_addr, r);
+        }
+        sm100::tmem_st_wait();
+        l *= alpha;
+      }
+      if (grow) m_used = m_blk;
+      const float m_ref = m_used == -INFINITY ? 0.f : m_used;
+      float sum = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = exp2f(fmaf(s[2 * i], p.scale_log2, -m_ref));
+        const float p1 = exp2f(fmaf(s[2 * i + 1], p.scale_log2, -m_ref));
+        sum += p0 + p1;
+        pk[i] = pack2<T>(p0, p1);
+      }
+      l += sum;
+      const uint32_t p_tmem = tmem + S_COL0 + 128u * (uint32_t)(j % 3) + lane_addr;
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = pk[i];
+        sm100::tmem_st_32x32b_x32(p_tmem, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = pk[32 + i];
+        sm100::tmem_st_32x32b_x32(p_tmem + 32, r);
+      }
+      sm100::tmem_st_wait();
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&p_full[j % 3]);
+    }
+    // Epilogue: O / l, written as this row's D contiguous elements.
+    if (ok && nkv > 0)
+      ok = sm100::mbar_wait(&pv_done[(nkv - 1) % 3], (uint32_t)(((nkv - 1) / 3) & 1), abort_flag, p.err);
+    sm100::tc_fence_after();
+    if (ok) {
+      const float inv = 1.f / l;  // l == 0 (fully masked row) gives NaN, as torch does
+      T* orow = reinterpret_cast<T*>(p.o) + (int64_t)b * p.o_b + (int64_t)hq * p.o_h + (int64_t)row * p.o_s;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        if (nkv > 0) {
+          sm100::tmem_ld_32x32b_x32(tmem + O_COL + c * 32 + lane_addr, r);
+          sm100::tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        if (row < p.Sq) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            ew::Vec<T, 8> v;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v.v[e] = cvt<T>(__uint_as_float(r[i + e]) * inv);
+            *reinterpret_cast<ew::Vec<T, 8>*>(orow + c * 32 + i) = v;
+          }
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 5) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------ CUDA-core attention --------
+// One warp per query row, 4 rows per block sharing 32-key K / V tiles staged in shared memory
+// (rows padded by one element against bank conflicts).  Handles every dtype, head size up to
+// 256, strided tensors, additive masks, causal variants and GQA.  Accumulates in Acc.
+struct GenArgs {
+  const void *q, *k, *v, *mask;
+  int64_t q_b, q_h, q_s, k_b, k_h, k_s, v_b, v_h, v_s;
+  int64_t m_b, m_h, m_q, m_k;
+  int Dv;
+};
+
+constexpr int kGenRows = 4;
+constexpr int kGenKeys = 32;
+
+template <typename T, typename Acc>
+__global__ void __launch_bounds__(128) fmha_generic_kernel(GenArgs a, Params p) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  const int D = p.D, Dv = a.Dv;
+  Acc* Ks = reinterpret_cast<Acc*>(gsm);                  // [kGenKeys][D + 1]
+  Acc* Vs = Ks + kGenKeys * (D + 1);                       // [kGenKeys][Dv + 1]
+  Acc* Qs = Vs + kGenKeys * (Dv + 1);                      // [kGenRows][D]
+  Acc* Ps = Qs + kGenRows * D;                             // [kGenRows][kGenKeys]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nrb = (p.Sq + kGenRows - 1) / kGenRows;
+  const int rb = blockIdx.x % nrb;
+  const int bh = blockIdx.x / nrb;
+  const int b = bh / p.Hq, hq = bh % p.Hq, hkv = hq / p.group;
+  const int row = rb * kGenRows + warp;
+  const bool row_ok = row < p.Sq;
+  const T* Q = reinterpret_cast<const T*>(a.q) + (int64_t)b * a.q_b + (int64_t)hq * a.q_h;
+  const T* K = reinterpret_cast<const T*>(a.k) + (int64_t)b * a.k_b + (int64_t)hkv * a.k_h;
+  const T* V = reinterpret_cast<const T*>(a.v) + (int64_t)b * a.v_b + (int64_t)hkv * a.v_h;
+  const T* M = a.mask ? reinterpret_cast<const T*>(a.mask) + (int64_t)b * a.m_b + (int64_t)hq * a.m_h : nullptr;
+  const Acc scale = Acc(p.scale_log2) / Acc(kLog2e);
+  for (int d = lane; d < D; d += 32) Qs[warp * D + d] = row_ok ? cvt<Acc>(Q[(int64_t)row * a.q_s + d]) : Acc(0);
+  const int off = p.causal == 2 ? p.Skv - p.Sq : 0;
+  const int kmax = p.causal ? min(p.Skv - 1, row + off) : p.Skv - 1;
+  // The block's largest allowed key bounds the KV loop (causal skip).
+  int block_kmax = p.Skv - 1;
+  if (p.causal) block_kmax = min(p.Skv - 1, rb * kGenRows + kGenRows - 1 + off);
+  Acc m = -INFINITY, l = 0;
+  Acc acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0;
+  for (int k0 = 0; k0 <= block_kmax; k0 += kGenKeys) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kGenKeys * D; i += blockDim.x) {
+      const int kk = i / D, d = i % D;
+      Ks[kk * (D + 1) + d] = (k0 + kk < p.Skv) ? cvt<Acc>(K[(int64_t)(k0 + kk) * a.k_s + d]) : Acc(0);
+    }
+    for (int i = threadIdx.x; i < kGenKeys * Dv; i += blockDim.x) {
+      const int kk = i / Dv, d = i % Dv;
+      Vs[kk * (Dv + 1) + d] = (k0 + kk < p.Skv) ? cvt<Acc>(V[(int64_t)(k0 + kk) * a.v_s + d]) : Acc(0);
+    }
+    __syncthreads();
+    // lane = key within the tile
+    const int key = k0 + lane;
+    Acc sc = -INFINITY;
+    if (row_ok && key <= kmax) {
+      Acc dot = 0;
+      for (int d = 0; d < D; ++d) dot += Qs[warp * D + d] * Ks[lane * (D + 1) + d];
+      sc = dot * scale;
+      if (M != nullptr) sc += cvt<Acc>(M[(int64_t)row * a.m_q + (int64_t)key * a.m_k]);
+    }
+    Acc mt = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mt = fmax(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+    const Acc m_new = fmax(m, mt);
+    const Acc m_ref = m_new == -INFINITY ? Acc(0) : m_new;
+    const Acc alpha = exp(m - m_ref);
+    const Acc pj = exp(sc - m_ref);
+    Acc ps = pj;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    l = l * alpha + ps;
+    m = m_new;
+    Ps[warp * kGenKeys + lane] = pj;
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = lane + 32 * i;
+      if (d < Dv) {
+        Acc s2 = acc[i] * alpha;
+        for (int kk = 0; kk < kGenKeys; ++kk) s2 += Ps[warp * kGenKeys + kk] * Vs[kk * (Dv + 1) + d];
+        acc[i] = s2;
+      }
+    }
+    __syncwarp();
+  }
+  if (row_ok) {
+    T* O = reinterpret_cast<T*>(p.o) + (int64_t)b * p.o_b + (int64_t)hq * p.o_h + (int64_t)row * p.o_s;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = lane + 32 * i;
+      if (d < Dv) O[d] = cvt<T>(acc[i] / l);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------- host -------
+template <typename T, int D>
+int launch_tc(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, Params p, CUtensorMapDataType tdt,
+              cudaStream_t st) {
+  using S = Smem<D>;
+  const int es = sizeof(T);
+  CUtensorMap tq, tk, tv;
+  int rc;
+  // dims (D, S, H, B); strides in bytes for S, H, B.  A size-1 dim's stride is never used to
+  // step, so it is replaced by a dense one (TMA wants every stride a positive multiple of 16).
+  auto sb = [&](const NtbTensor* t, int d) -> uint64_t {
+    if (t->shape[d] != 1) return (uint64_t)t->stride[d] * es;
+    uint64_t dense = (uint64_t)es;
+    for (int i = d + 1; i < 4; ++i) dense *= (uint64_t)t->shape[i];
+    return (dense + 15) / 16 * 16;
+  };
+  if ((rc = tma::encode_4d(&tq, tdt, q->data, p.D, p.Sq, p.Hq, p.B, sb(q, 2), sb(q, 1), sb(q, 0), 64, BLK)) != NTB_OK)
+    return rc;
+  if ((rc = tma::encode_4d(&tk, tdt, k->data, p.D, p.Skv, p.Hkv, p.B, sb(k, 2), sb(k, 1), sb(k, 0), 64, BLK)) !=
+      NTB_OK)
+    return rc;
+  if ((rc = tma::encode_4d(&tv, tdt, v->data, p.D, p.Skv, p.Hkv, p.B, sb(v, 2), sb(v, 1), sb(v, 0), 64, BLK)) !=
+      NTB_OK)
+    return rc;
+  auto kernel = fmha_tc_kernel<T, D>;
+  static std::atomic<uint64_t> attr_set{0};
+  const uint64_t bit = 1ull << (current_device() & 63);
+  if (!(attr_set.load() & bit)) {
+    NTB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    attr_set.fetch_or(bit);
+  }
+  const int64_t grid = (int64_t)p.B * p.Hq * p.nq;
+  NTB_UNSUP(grid <= 0x7fffffffLL, "attention grid too large");
+  kernel<<<(unsigned)grid, kThreads, S::TOTAL, st>>>(tq, tk, tv, p);
+  NTB_LAUNCH_CHECK();
+  return NTB_OK;
+}
+
+template <typename T>
+int launch_generic(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask, Params p,
+                   int Dv, cudaStream_t st) {
+  using Acc = typename std::conditional<std::is_same<T, double>::value, double, float>::type;
+  GenArgs a;
+  a.q = q->data;
+  a.k = k->data;
+  a.v = v->data;
+  a.mask = mask ? mask->data : nullptr;
+  a.q_b = q->stride[0]; a.q_h = q->stride[1]; a.q_s = q->stride[2];
+  a.k_b = k->stride[0]; a.k_h = k->stride[1]; a.k_s = k->stride[2];
+  a.v_b = v->stride[0]; a.v_h = v->stride[1]; a.v_s = v->stride[2];
+  if (mask) {
+    a.m_b = mask->stride[0]; a.m_h = mask->stride[1]; a.m_q = mask->stride[2]; a.m_k = mask->stride[3];
+  } else {
+    a.m_b = a.m_h = a.m_q = a.m_k = 0;
+  }
+  a.Dv = Dv;
+  const size_t smem = sizeof(Acc) * ((size_t)kGenKeys * (p.D + 1) + (size_t)kGenKeys * (Dv + 1) +
+                                     (size_t)kGenRows * p.D + (size_t)kGenRows * kGenKeys);
+  auto kernel = fmha_generic_kernel<T, Acc>;
+  if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t grid = (int64_t)p.B * p.Hq * ((p.Sq + kGenRows - 1) / kGenRows);
+  NTB_UNSUP(grid <= 0x7fffffffLL, "attention grid too large");
+  kernel<<<(unsigned)grid, 128, smem, st>>>(a, p);
+  NTB_LAUNCH_CHECK();
+  return NTB_OK;
+}
+
+bool tma_attn_ok(const NtbTensor* t, int es) {
+  if (reinterpret_cast<uintptr_t>(t->data) % 16 != 0) return false;
+  if (t->stride[3] != 1) return false;
+  for (int d = 0; d < 3; ++d)
+    if (t->shape[d] > 1 && !tma::stride_ok(t->stride[d] * es)) return false;
+  return true;
+}
+
+}  // namespace fmha
+}  // namespace ntb
+
+extern "C" int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+                        const NtbTensor* o, double scale, int causal_variant, void* stream) {
+  using namespace ntb;
+  using namespace ntb::fmha;
+  int rc;
+  if ((rc = check_tensor(q, "query")) != NTB_OK) return rc;
+  if ((rc = check_tensor(k, "key")) != NTB_OK) return rc;
+  if ((rc = check_tensor(v, "value")) != NTB_OK) return rc;
+  if ((rc = check_tensor(o, "output")) != NTB_OK) return rc;
+  if (mask != nullptr && (rc = check_tensor(mask, "attn_mask")) != NTB_OK) return rc;
+  NTB_ARG(q->ndim == 4 && k->ndim == 4 && v->ndim == 4 && o->ndim == 4, "q, k, v, out must be 4-D [B, H, S, D]");
+  NTB_ARG(k->shape[0] == q->shape[0] && v->shape[0] == q->shape[0], "batch sizes differ");
+  NTB_ARG(k->shape[1] == v->shape[1] && k->shape[1] > 0 && q->shape[1] % k->shape[1] == 0,
+          "query heads must be a multiple of key/value heads");
+  NTB_ARG(k->shape[2] == v->shape[2], "key and value lengths differ");
+  NTB_ARG(k->shape[3] == q->shape[3], "query and key head dims differ");
+  NTB_ARG(o->shape[0] == q->shape[0] && o->shape[1] == q->shape[1] && o->shape[2] == q->shape[2] &&
+              o->shape[3] == v->shape[3],
+          "output shape must be [B, Hq, Sq, Dv]");
+  NTB_ARG(o->stride[3] == 1 || o->shape[3] == 1, "output inner stride must be 1");
+  NTB_UNSUP(k->dtype == q->dtype && v->dtype == q->dtype && o->dtype == q->dtype, "q, k, v, out must share one dtype");
+  NTB_UNSUP(dtype_is_float(q->dtype), "attention needs floating-point tensors");
+  NTB_ARG(causal_variant >= 0 && causal_variant <= 2, "bad causal variant %d", causal_variant);
+  if (mask != nullptr) {
+    NTB_ARG(mask->ndim == 4 && mask->shape[0] == q->shape[0] && mask->shape[1] == q->shape[1] &&
+                mask->shape[2] == q->shape[2] && mask->shape[3] == k->shape[2],
+            "attn_mask must be expanded to [B, Hq, Sq, Skv]");
+    NTB_UNSUP(mask->dtype == q->dtype, "attn_mask dtype must equal the query dtype");
+  }
+  NTB_UNSUP(q->shape[3] <= 256 && v->shape[3] <= 256, "head_dim above 256 is not supported");
+  Params p = {};
+  p.B = (int)q->shape[0];
+  p.Hq = (int)q->shape[1];
+  p.Sq = (int)q->shape[2];
+  p.D = (int)q->shape[3];
+  p.Hkv = (int)k->shape[1];
+  p.Skv = (int)k->shape[2];
+  p.group = p.Hq / p.Hkv;
+  p.causal = causal_variant;
+  p.nq = (p.Sq + BLK - 1) / BLK;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.o = o->data;
+  p.o_b = o->stride[0];
+  p.o_h = o->stride[1];
+  p.o_s = o->stride[2];
+  p.err = device_error_ptr();
+  if ((int64_t)p.B * p.Hq * p.Sq == 0 || v->shape[3] == 0) return NTB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool half_t = q->dtype == NTB_BF16 || q->dtype == NTB_F16;
+  const int es = dtype_size(q->dtype);
+  const bool tc = half_t && mask == nullptr && (p.D == 64 || p.D == 128) && v->shape[3] == p.D && p.Skv > 0 &&
+                  tma_attn_ok(q, es) && tma_attn_ok(k, es) && tma_attn_ok(v, es) &&
+                  (reinterpret_cast<uintptr_t>(o->data) % 16 == 0) && (p.o_s % 8 == 0) &&
+                  (p.o_h % 8 == 0 || p.Hq == 1) && (p.o_b % 8 == 0 || p.B == 1);
+  if (tc) {
+    if (q->dtype == NTB_BF16)
+      return p.D == 128 ? launch_tc<__nv_bfloat16, 128>(q, k, v, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st)
+                        : launch_tc<__nv_bfloat16, 64>(q, k, v, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
+    return p.D == 128 ? launch_tc<__half, 128>(q, k, v, p, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st)
+                      : launch_tc<__half, 64>(q, k, v, p, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
+  }
+  NTB_DISPATCH_FLOAT(q->dtype, return launch_generic<scalar_t>(q, k, v, mask, p, (int)v->shape[3], st));
+  return NTB_OK;
+}

@@ -1,0 +1,548 @@
+// ntb_gemm: mm / bmm / addmm / matmul.
+//
+// Reference (ntops kernels/mm.py:54-65, kernels/bmm.py:8-43, kernels/addmm.py:64-67): an
+// output-tile grid whose programs run a K loop of tl.dot into an fp32 accumulator, addmm adding
+// beta * input + alpha * acc in the epilogue; fp32 operands use TF32 unless torch's float32
+// matmul precision is "highest" (torch/utils.py:218-222).
+//
+// sm_100a design (bf16 / fp16, and fp32 as TF32):
+//   * persistent kernel, one 192-thread CTA per SM, static tile schedule (tile = blockIdx.x +
+//     i * gridDim.x) rasterised in bands of 8 M-blocks so concurrently running tiles share A
+//     rows and B columns in L2;
+//   * warp 0 issues TMA loads (128-byte swizzle, zero fill past the edges) into a STAGES-deep
+//     ring of shared-memory stages guarded by full/empty mbarriers;
+//   * warp 1 allocates 2 x BN TMEM columns (a double-buffered 128 x BN fp32 accumulator) and one
+//     lane issues tcgen05.mma (M=128, N=BN, K=16 / 8) for each stage, releasing the stage with
+//     tcgen05.commit;
+//   * warps 2-5 drain the other accumulator buffer with tcgen05.ld (one TMEM lane = one output
+//     row per thread), apply alpha / beta * C, convert and store, so the epilogue of tile i
+//     overlaps the main loop of tile i+1.
+// Operands may be K-major or M/N-major (transpose bits of the instruction descriptor) for
+// 16-bit types; TF32 takes K-major operands.  Shapes or strides that TMA cannot address
+// (unaligned rows) and IEEE fp32 / fp64 run on the CUDA-core kernel at the end of this file.
+#include <atomic>
+#include <type_traits>
+
+#include "elementwise.cuh"
+#include "sm100.cuh"
+#include "tma.cuh"
+
+namespace ntb {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int kRowBytes = 128;  // one swizzle atom row: BK elements of the operand type
+constexpr int kThreads = 192;
+
+struct Params {
+  int M, N, K, batch;
+  int mblocks, nblocks, kblocks, tiles;
+  int a_mn, b_mn;  // operand is MN-major (else K-major)
+  void* d;
+  int64_t d_bs, d_ms;  // output: batch and row strides (unit column stride)
+  const void* c;       // optional addend (same dtype as d), any strides (0 = broadcast)
+  int64_t c_bs, c_ms, c_ns;
+  float alpha, beta;
+  unsigned int* err;
+};
+
+template <int BN, int STAGES, int ESIZE>
+struct Smem {
+  static constexpr int BK = kRowBytes / ESIZE;           // K elements per stage
+  static constexpr int A_BYTES = BM * kRowBytes;         // 16 KB
+  static constexpr int B_BYTES = BN * kRowBytes;         // 16 / 32 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = TILE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, const Params& p, int& b, int& mb, int& nb) {
+  const int per_batch = p.mblocks * p.nblocks;
+  b = tile / per_batch;
+  int t = tile - b * per_batch;
+  constexpr int G = 8;  // M-blocks per raster band
+  const int band = t / (G * p.nblocks);
+  const int m0 = band * G;
+  const int gm = min(G, p.mblocks - m0);
+  const int r = t - band * G * p.nblocks;
+  mb = m0 + r % gm;
+  nb = r / gm;
+}
+
+template <typename TD>
+__device__ __forceinline__ void store_row_chunk(const Params& p, TD* drow, const TD* crow, int col0,
+                                                const float (&v)[32]) {
+  // drow / crow point at element (row, 0) of D / C; col0 is the first column of this chunk.
+  float o[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) o[j] = p.alpha * v[j];
+  if (crow != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int col = col0 + j;
+      if (col < p.N) o[j] += p.beta * cvt<float>(crow[(int64_t)col * p.c_ns]);
+    }
+  }
+  const bool full = col0 + 32 <= p.N;
+  constexpr int V = 16 / sizeof(TD);
+  if (full && ((reinterpret_cast<uintptr_t>(drow + col0) % 16) == 0)) {
+#pragma unroll
+    for (int j = 0; j < 32; j += V) {
+      ew::Vec<TD, V> vv;
+#pragma unroll
+      for (int e = 0; e < V; ++e) vv.v[e] = cvt<TD>(o[j + e]);
+      *reinterpret_cast<ew::Vec<TD, V>*>(drow + col0 + j) = vv;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < p.N) drow[col0 + j] = cvt<TD>(o[j]);
+  }
+}
+
+// T: operand element type (__half / __nv_bfloat16 / float for TF32); TD: output type.
+template <typename T, typename TD, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   Params p) {
+  using S = Smem<BN, STAGES, sizeof(T)>;
+  constexpr int BK = S::BK;
+  constexpr bool kTF32 = sizeof(T) == 4;
+  constexpr int UMMA_K = kTF32 ? 8 : 16;  // 32 bytes of K per instruction
+  constexpr int KSTEPS = BK / UMMA_K;     // 4
+  constexpr uint32_t kFormat = kTF32 ? 2u : (std::is_same<T, __nv_bfloat16>::value ? 1u : 0u);
+  constexpr int TMEM_COLS = 2 * BN;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* done_bar = tmem_empty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tmem_full[a], 1);
+      sm100::mbar_init(&tmem_empty[a], 128);
+    }
+    sm100::mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+    sm100::tma_prefetch_desc(&tma_a);
+    sm100::tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_base_slot, TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer ----
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;        // bit s: stage s was armed at least once
+      uint32_t last_parity = 0;  // bit s: parity of stage s's last armed phase
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+        int b, mb, nb;
+        tile_coords(tile, p, b, mb, nb);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!sm100::mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          sm100::mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
+          armed |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          uint8_t* a_dst = sA + stage * S::A_BYTES;
+          uint8_t* b_dst = sB + stage * S::B_BYTES;
+          if (!p.a_mn) {
+            sm100::tma_load_3d(a_dst, &tma_a, &full[stage], kb * BK, mb * BM, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              sm100::tma_load_3d(a_dst + j * BK * kRowBytes, &tma_a, &full[stage], mb * BM + j * 64, kb * BK, b);
+          }
+          if (!p.b_mn) {
+            sm100::tma_load_3d(b_dst, &tma_b, &full[stage], kb * BK, nb * BN, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              sm100::tma_load_3d(b_dst + j * BK * kRowBytes, &tma_b, &full[stage], nb * BN + j * 64, kb * BK, b);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Unwind: every load this thread issued must land before the CTA may exit.
+      for (int s = 0; s < STAGES; ++s)
+        if (armed & (1u << s)) sm100::mbar_wait_unwind(&full[s], (last_parity >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------- MMA issuer ----
+    constexpr uint32_t idesc_kk = sm100::instr_desc(kFormat, false, false, BM, BN);
+    const uint32_t idesc = idesc_kk | ((p.a_mn ? 1u : 0u) << 15) | ((p.b_mn ? 1u : 0u) << 16);
+    // Byte advance of one UMMA_K step inside a stage, and the descriptors' LBO / SBO.
+    const uint32_t a_kstep = p.a_mn ? UMMA_K * kRowBytes : UMMA_K * (uint32_t)sizeof(T);
+    const uint32_t b_kstep = p.b_mn ? UMMA_K * kRowBytes : UMMA_K * (uint32_t)sizeof(T);
+    const uint32_t a_lbo = p.a_mn ? BK * kRowBytes : 16, a_sbo = 1024;
+    const uint32_t b_lbo = p.b_mn ? BK * kRowBytes : 16, b_sbo = 1024;
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+      if (!sm100::mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+      sm100::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < p.kblocks; ++kb) {
+        if (!sm100::mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a0 = sm100::smem_u32(sA + stage * S::A_BYTES);
+          const uint32_t b0 = sm100::smem_u32(sB + stage * S::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < KSTEPS; ++k) {
+            const uint64_t ad = sm100::smem_desc(a0 + k * a_kstep, a_lbo, a_sbo);
+            const uint64_t bd = sm100::smem_desc(b0 + k * b_kstep, b_lbo, b_sbo);
+            if (kTF32)
+              sm100::mma_tf32(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            else
+              sm100::mma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          sm100::mma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) sm100::mma_commit(&tmem_full[acc]);
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    // Unwind: wait until every MMA issued by this warp has completed.
+    if (lane == 0) {
+      sm100::mma_commit(done_bar);
+      sm100::mbar_wait_unwind(done_bar, 0);
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------------------- epilogue ----
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+      int b, mb, nb;
+      tile_coords(tile, p, b, mb, nb);
+      if (!sm100::mbar_wait(&tmem_full[acc], acc_phase, abort_flag, p.err)) break;
+      sm100::tc_fence_after();
+      const int row = mb * BM + row_in_tile;
+      TD* drow = reinterpret_cast<TD*>(p.d) + (int64_t)b * p.d_bs + (int64_t)row * p.d_ms;
+      const TD* crow = nullptr;
+      if (p.c != nullptr && p.beta != 0.f)
+        crow = reinterpret_cast<const TD*>(p.c) + (int64_t)b * p.c_bs + (int64_t)row * p.c_ms;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t r[32];
+        sm100::tmem_ld_32x32b_x32(tmem_base + acc * BN + ch * 32 + ((uint32_t)(q * 32) << 16), r);
+        sm100::tmem_ld_wait();
+        const int col0 = nb * BN + ch * 32;
+        if (row < p.M && col0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          store_row_chunk<TD>(p, drow, crow, col0, v);
+        }
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&tmem_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------- CUDA-core fallback ------
+// 64 x 64 output tile per 256-thread block, 4 x 4 outputs per thread, K staged through shared
+// memory 16 at a time; accumulates in Acc (fp32, or fp64 for fp64 operands).  Handles any
+// strides, K = 0, IEEE fp32 and fp64.
+struct SimtArgs {
+  const void* a;
+  const void* b;
+  int64_t a_bs, a_ms, a_ks, b_bs, b_ks, b_ns;
+};
+
+template <typename T, typename Acc>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(SimtArgs s, Params p) {
+  __shared__ Acc As[16][64 + 1];
+  __shared__ Acc Bs[16][64 + 1];
+  const int bz = blockIdx.z;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  const T* A = reinterpret_cast<const T*>(s.a) + (int64_t)bz * s.a_bs;
+  const T* B = reinterpret_cast<const T*>(s.b) + (int64_t)bz * s.b_bs;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  Acc acc[4][4] = {};
+  for (int k0 = 0; k0 < p.K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int kk = i / 64, mm = i % 64;
+      const int gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < p.M && gk < p.K) ? cvt<Acc>(A[(int64_t)gm * s.a_ms + (int64_t)gk * s.a_ks]) : Acc(0);
+      const int gn = n0 + mm;
+      Bs[kk][mm] = (gn < p.N && gk < p.K) ? cvt<Acc>(B[(int64_t)gk * s.b_ks + (int64_t)gn * s.b_ns]) : Acc(0);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      Acc av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] += av[i] * bv[j];
+    }
+    __syncthreads();
+  }
+  T* D = reinterpret_cast<T*>(p.d) + (int64_t)bz * p.d_bs;
+  const T* C = p.c ? reinterpret_cast<const T*>(p.c) + (int64_t)bz * p.c_bs : nullptr;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + ty * 4 + i;
+    if (gm >= p.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tx * 4 + j;
+      if (gn >= p.N) continue;
+      Acc o = Acc(p.alpha) * acc[i][j];
+      if (C != nullptr && p.beta != 0.f) o += Acc(p.beta) * cvt<Acc>(C[(int64_t)gm * p.c_ms + (int64_t)gn * p.c_ns]);
+      D[(int64_t)gm * p.d_ms + gn] = cvt<T>(o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------- host -------
+struct Operand {
+  int64_t bs, s_outer, s_k;  // batch stride, stride along M (A) / N (B), stride along K
+};
+
+template <typename T, typename TD, int BN, int STAGES>
+int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& oa, const Operand& ob,
+              CUtensorMapDataType tdt, cudaStream_t st) {
+  using S = Smem<BN, STAGES, sizeof(T)>;
+  constexpr int BK = S::BK;
+  const int es = sizeof(T);
+  CUtensorMap ta, tb;
+  int rc;
+  const uint64_t B = (uint64_t)p.batch;
+  // A: K-major -> dims (K, M, B), box (BK, BM); MN-major -> dims (M, K, B), box (64, BK).
+  if (!p.a_mn)
+    rc = tma::encode_3d(&ta, tdt, a->data, p.K, p.M, B, oa.s_outer * es, (B > 1 ? oa.bs : oa.s_outer * p.M) * es,
+                        BK, BM);
+  else
+    rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, B, oa.s_k * es, (B > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
+  if (rc != NTB_OK) return rc;
+  if (!p.b_mn)
+    rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, B, ob.s_outer * es, (B > 1 ? ob.bs : ob.s_outer * p.N) * es,
+                        BK, BN);
+  else
+    rc = tma::encode_3d(&tb, tdt, bm->data, p.N, p.K, B, ob.s_k * es, (B > 1 ? ob.bs : ob.s_k * p.K) * es, 64, BK);
+  if (rc != NTB_OK) return rc;
+  p.kblocks = (p.K + BK - 1) / BK;
+  p.mblocks = (p.M + BM - 1) / BM;
+  p.nblocks = (p.N + BN - 1) / BN;
+  p.tiles = p.mblocks * p.nblocks * p.batch;
+  auto kernel = gemm_tc_kernel<T, TD, BN, STAGES>;
+  static std::atomic<uint64_t> attr_set{0};  // bit per device; setting twice is harmless
+  const int dev = current_device();
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set.load() & bit)) {
+    NTB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    attr_set.fetch_or(bit);
+  }
+  const int grid = p.tiles < sm_count() ? p.tiles : sm_count();
+  kernel<<<grid, kThreads, S::TOTAL, st>>>(ta, tb, p);
+  NTB_LAUNCH_CHECK();
+  return NTB_OK;
+}
+
+template <typename T>
+int launch_simt(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& oa, const Operand& ob,
+                cudaStream_t st) {
+  SimtArgs s;
+  s.a = a->data;
+  s.b = bm->data;
+  s.a_bs = oa.bs;
+  s.a_ms = oa.s_outer;
+  s.a_ks = oa.s_k;
+  s.b_bs = ob.bs;
+  s.b_ns = ob.s_outer;
+  s.b_ks = ob.s_k;
+  dim3 grid((p.N + 63) / 64, (p.M + 63) / 64, p.batch);
+  NTB_UNSUP(grid.y <= 65535 && grid.z <= 65535, "problem too large for the CUDA-core GEMM");
+  using Acc = typename std::conditional<std::is_same<T, double>::value, double, float>::type;
+  gemm_simt_kernel<T, Acc><<<grid, 256, 0, st>>>(s, p);
+  NTB_LAUNCH_CHECK();
+  return NTB_OK;
+}
+
+// Normalises a 2-D or 3-D descriptor to [batch, rows, cols] sizes and strides.
+bool as3d(const NtbTensor* t, int64_t* sz, int64_t* str) {
+  if (t->ndim == 2) {
+    sz[0] = 1;
+    str[0] = 0;
+    sz[1] = t->shape[0];
+    sz[2] = t->shape[1];
+    str[1] = t->stride[0];
+    str[2] = t->stride[1];
+    return true;
+  }
+  if (t->ndim == 3) {
+    for (int i = 0; i < 3; ++i) {
+      sz[i] = t->shape[i];
+      str[i] = t->stride[i];
+    }
+    return true;
+  }
+  return false;
+}
+
+template <typename T>
+bool tma_operand_ok(const NtbTensor* t, const Operand& o, bool mn_major, int64_t outer, int64_t kdim,
+                    int64_t batch) {
+  const int es = sizeof(T);
+  if (reinterpret_cast<uintptr_t>(t->data) % 16 != 0) return false;
+  const int64_t other = mn_major ? o.s_k : o.s_outer;  // the non-unit stride
+  if (!tma::stride_ok(other * es)) return false;
+  if (batch > 1 && !tma::stride_ok(o.bs * es)) return false;
+  (void)outer;
+  (void)kdim;
+  return true;
+}
+
+}  // namespace gemm
+}  // namespace ntb
+
+extern "C" int ntb_gemm(const NtbTensor* a, const NtbTensor* bm, const NtbTensor* c, const NtbTensor* d,
+                        double alpha, double beta, int precision, void* stream) {
+  using namespace ntb;
+  using namespace ntb::gemm;
+  int rc;
+  if ((rc = check_tensor(a, "mat1")) != NTB_OK) return rc;
+  if ((rc = check_tensor(bm, "mat2")) != NTB_OK) return rc;
+  if ((rc = check_tensor(d, "out")) != NTB_OK) return rc;
+  if (c != nullptr && (rc = check_tensor(c, "input")) != NTB_OK) return rc;
+  int64_t as[3], ast[3], bs[3], bst[3], ds[3], dst[3];
+  NTB_ARG(as3d(a, as, ast) && as3d(bm, bs, bst) && as3d(d, ds, dst), "operands must be 2-D or 3-D");
+  NTB_ARG(as[0] == bs[0] && as[0] == ds[0], "batch sizes differ (%lld, %lld, %lld)", (long long)as[0],
+          (long long)bs[0], (long long)ds[0]);
+  NTB_ARG(as[2] == bs[1], "inner dimensions differ (%lld vs %lld)", (long long)as[2], (long long)bs[1]);
+  NTB_ARG(ds[1] == as[1] && ds[2] == bs[2], "output shape mismatch");
+  NTB_ARG(dst[2] == 1 || ds[2] == 1, "output must have a unit column stride");
+  NTB_UNSUP(a->dtype == bm->dtype, "mat1 and mat2 dtypes differ");
+  NTB_UNSUP(d->dtype == a->dtype, "output dtype must equal the operands' dtype");
+  NTB_UNSUP(dtype_is_float(a->dtype), "gemm needs floating-point operands");
+  NTB_ARG(as[1] < (1LL << 31) && bs[2] < (1LL << 31) && as[2] < (1LL << 31) && as[0] < (1LL << 31),
+          "dimension too large");
+
+  Params p = {};
+  p.batch = (int)as[0];
+  p.M = (int)as[1];
+  p.K = (int)as[2];
+  p.N = (int)bs[2];
+  p.d = d->data;
+  p.d_bs = dst[0];
+  p.d_ms = dst[1];
+  p.alpha = (float)alpha;
+  p.beta = (float)beta;
+  p.err = device_error_ptr();
+  if (c != nullptr) {
+    NTB_UNSUP(c->dtype == d->dtype, "input (addend) dtype must equal the output dtype");
+    // c is broadcast to [batch, M, N] through its strides (caller expands it).
+    int64_t cs[3], cst[3];
+    NTB_ARG(as3d(c, cs, cst), "input (addend) must be 2-D or 3-D");
+    NTB_ARG(cs[0] == ds[0] && cs[1] == ds[1] && cs[2] == ds[2], "input (addend) must be expanded to the output shape");
+    p.c = c->data;
+    p.c_bs = cst[0];
+    p.c_ms = cst[1];
+    p.c_ns = cst[2];
+  }
+  if ((int64_t)p.M * p.N * p.batch == 0) return NTB_OK;
+  Operand oa{ast[0], ast[1], ast[2]};
+  Operand ob{bst[0], bst[2], bst[1]};
+  cudaStream_t st = (cudaStream_t)stream;
+
+  // Operand majorness: unit stride along K -> K-major, unit stride along M / N -> MN-major.
+  const bool a_k = oa.s_k == 1 || p.K == 1, a_mn = oa.s_outer == 1 || p.M == 1;
+  const bool b_k = ob.s_k == 1 || p.K == 1, b_mn = ob.s_outer == 1 || p.N == 1;
+  p.a_mn = a_k ? 0 : 1;
+  p.b_mn = b_k ? 0 : 1;
+  const bool a_ok_layout = a_k || a_mn, b_ok_layout = b_k || b_mn;
+
+  const bool half_t = a->dtype == NTB_F16 || a->dtype == NTB_BF16;
+  const bool tf32 = a->dtype == NTB_F32 && precision == NTB_PRECISION_TF32;
+  bool use_tc = p.K > 0 && a_ok_layout && b_ok_layout && (half_t || (tf32 && !p.a_mn && !p.b_mn));
+  if (use_tc) {
+    if (a->dtype == NTB_F16) {
+      use_tc = tma_operand_ok<__half>(a, oa, p.a_mn, p.M, p.K, p.batch) &&
+               tma_operand_ok<__half>(bm, ob, p.b_mn, p.N, p.K, p.batch);
+    } else if (a->dtype == NTB_BF16) {
+      use_tc = tma_operand_ok<__nv_bfloat16>(a, oa, p.a_mn, p.M, p.K, p.batch) &&
+               tma_operand_ok<__nv_bfloat16>(bm, ob, p.b_mn, p.N, p.K, p.batch);
+    } else {
+      use_tc = tma_operand_ok<float>(a, oa, false, p.M, p.K, p.batch) &&
+               tma_operand_ok<float>(bm, ob, false, p.N, p.K, p.batch);
+    }
+  }
+  if (use_tc) {
+    const bool wide = p.N > 128;
+    switch (a->dtype) {
+      case NTB_BF16:
+        return wide ? launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st)
+                    : launch_tc<__nv_bfloat16, __nv_bfloat16, 128, 6>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
+      case NTB_F16:
+        return wide ? launch_tc<__half, __half, 256, 4>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st)
+                    : launch_tc<__half, __half, 128, 6>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
+      default:
+        return wide ? launch_tc<float, float, 256, 4>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, st)
+                    : launch_tc<float, float, 128, 6>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, st);
+    }
+  }
+  NTB_DISPATCH_FLOAT(a->dtype, return launch_simt<scalar_t>(a, bm, p, oa, ob, st));
+  return NTB_OK;
+}

@@ -1,0 +1,131 @@
+"""Parity of scaled_dot_product_attention against the oracle.
+
+The reference grid (tests/test_scaled_dot_product_attention.py:15-92: mask None / bool /
+float(0 or -inf), causal, scale, fp32 / fp16, KV cache, causal variant; seq 1-512, head_dim
+32 / 64, GQA always on; tolerances fp32 1e-2, fp16 2.5e-2) runs mostly on the CUDA-core kernel;
+the bf16 / fp16 head_dim 64 / 128 cases without a mask run on the tcgen05 kernel, including
+ragged sequence lengths, Sq != Skv, lower-right causal, GQA and strided [B, S, H, D] views.
+"""
+
+import itertools
+import math
+import random
+
+import pytest
+import torch
+
+import oracle.ops as O
+from ntops_b200.kernels.scaled_dot_product_attention import CausalVariant
+from tests.utils import assert_close
+
+pytestmark = pytest.mark.gpu
+
+nt = pytest.importorskip("ntops_b200.torch") if torch.cuda.is_available() else None
+DEV = "cuda"
+
+
+def _reference_grid():
+    r = random.Random(99)
+    out = []
+    for mask_t, causal, scale, dtype, kv, variant in itertools.product(
+        (None, torch.bool, torch.float32), (False, True), (None, r.uniform(0.05, 0.5)),
+        (torch.float32, torch.float16), (False, True), (None, CausalVariant.LOWER_RIGHT, CausalVariant.UPPER_LEFT)):
+        if mask_t is not None and causal:
+            continue
+        b, hq = r.randint(1, 4), 2 ** r.randint(1, 5)
+        sq, d = r.randint(1, 512), r.choice([32, 64])
+        hkv = 2 ** r.randint(1, int(math.log2(hq)))
+        skv = r.randint(1, 512)
+        if variant == CausalVariant.LOWER_RIGHT and sq > skv:
+            continue
+        out.append((b, hq, sq, d, hkv, skv, mask_t, causal, scale, variant, kv, dtype))
+    return out
+
+
+def _tol(dtype):
+    return {torch.float32: (1e-2, 1e-2), torch.float16: (2.5e-2, 2.5e-2), torch.bfloat16: (2.5e-2, 2.5e-2)}[dtype]
+
+
+@pytest.mark.parametrize("b,hq,sq,d,hkv,skv,mask_t,causal,scale,variant,with_kv,dtype", _reference_grid())
+def test_reference_grid(b, hq, sq, d, hkv, skv, mask_t, causal, scale, variant, with_kv, dtype):
+    q = torch.randn((b, hq, sq, d)).to(dtype)
+    k = torch.randn((b, hkv, skv, d)).to(dtype)
+    v = torch.randn((b, hkv, skv, d)).to(dtype)
+    mask = None
+    if mask_t is not None:
+        mask = torch.rand((sq, skv)) > 0.5
+        if mask_t is not torch.bool:
+            mask = torch.where(mask, 0.0, float("-inf")).to(dtype)
+    kd, vd = k.to(DEV), v.to(DEV)
+    pk = pv = pks = pvs = None
+    if with_kv:
+        pk, pv = kd[:, :, -1:, :].clone(), vd[:, :, -1:, :].clone()
+        pks, pvs = kd[:, :, -1:, :], vd[:, :, -1:, :]
+        pks[...] = 0
+        pvs[...] = 0
+    got = nt.scaled_dot_product_attention(q.to(DEV), kd, vd, attn_mask=None if mask is None else mask.to(DEV),
+                                          is_causal=causal, scale=scale, enable_gqa=True, causal_variant=variant,
+                                          present_key=pk, present_value=pv, present_key_slot=pks,
+                                          present_value_slot=pvs)
+    cv = 2 if variant == CausalVariant.LOWER_RIGHT else 1
+    want = O.scaled_dot_product_attention(q, k, v, mask, causal, scale, cv)
+    assert_close(got, want, tol=_tol(dtype), equal_nan=True)
+
+
+TC_CASES = [
+    # b, hq, hkv, sq, skv, d, causal_variant (0 none)
+    (1, 2, 2, 128, 128, 128, 0),
+    (2, 4, 2, 256, 256, 128, 1),
+    (1, 8, 2, 300, 300, 128, 1),
+    (2, 4, 4, 200, 333, 64, 0),
+    (1, 4, 1, 129, 520, 128, 2),
+    (1, 2, 2, 1000, 1000, 64, 1),
+    (1, 4, 2, 64, 700, 128, 2),
+    (2, 2, 1, 512, 384, 128, 0),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("b,hq,hkv,sq,skv,d,cv", TC_CASES)
+def test_tensor_core_path(b, hq, hkv, sq, skv, d, cv, dtype):
+    q = torch.randn((b, hq, sq, d)).to(dtype)
+    k = torch.randn((b, hkv, skv, d)).to(dtype)
+    v = torch.randn((b, hkv, skv, d)).to(dtype)
+    got = nt.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV), is_causal=cv != 0, enable_gqa=True,
+                                          causal_variant=CausalVariant(cv) if cv else None)
+    want = O.scaled_dot_product_attention(q, k, v, None, cv != 0, None, cv if cv else 1)
+    assert_close(got, want, tol=(2e-2, 2e-2), equal_nan=True)
+
+
+def test_strided_bshd_views():
+    # Llama layout: q/k/v come from [B, S, H, D] projections and are attended as [B, H, S, D] views.
+    B, S, Hq, Hkv, D = 2, 256, 8, 2, 128
+    q = torch.randn((B, S, Hq, D)).to(torch.bfloat16)
+    k = torch.randn((B, S, Hkv, D)).to(torch.bfloat16)
+    v = torch.randn((B, S, Hkv, D)).to(torch.bfloat16)
+    got = nt.scaled_dot_product_attention(q.to(DEV).transpose(1, 2), k.to(DEV).transpose(1, 2),
+                                          v.to(DEV).transpose(1, 2), is_causal=True, enable_gqa=True)
+    want = O.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, True)
+    assert_close(got, want, tol=(2e-2, 2e-2))
+
+
+def test_large_logits_rescale():
+    # Rows whose max grows across KV blocks exercise the O rescale of the tcgen05 kernel.
+    B, H, S, D = 1, 2, 640, 128
+    q = torch.randn((B, H, S, D)) * 3
+    k = torch.randn((B, H, S, D)) * 3
+    k[:, :, 500:] *= 2.0
+    v = torch.randn((B, H, S, D))
+    qb, kb, vb = (t.to(torch.bfloat16) for t in (q, k, v))
+    got = nt.scaled_dot_product_attention(qb.to(DEV), kb.to(DEV), vb.to(DEV))
+    want = O.scaled_dot_product_attention(qb, kb, vb)
+    assert_close(got, want, tol=(2e-2, 2e-2))
+
+
+def test_asserts_like_reference():
+    q = torch.randn((1, 4, 8, 32), device=DEV)
+    k = torch.randn((1, 2, 8, 32), device=DEV)
+    with pytest.raises(AssertionError):
+        nt.scaled_dot_product_attention(q, k, k)  # GQA shapes without enable_gqa
+    with pytest.raises(AssertionError):
+        nt.scaled_dot_product_attention(q, q, q, dropout_p=0.1)
