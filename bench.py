@@ -296,6 +296,54 @@ def per_op_table(dev, peaks):
     return res
 
 
+# ----------------------------------------------------------------- single-op cases -------
+def run_case(name, reps):
+    """Runs one hot-path operator `reps` times on seeded inputs (for ncu captures of one kernel);
+    prints the median CUDA-event time of the launches."""
+    import ntops_b200.torch as nt
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rn(*shape, dt=torch.bfloat16, scale=1.0):
+        return (torch.randn(shape, generator=g, device=dev) * scale).to(dt)
+
+    if name == "gemm_gate":  # chain gate projection: [32768, 4096] x [4096, 14336]
+        a, b = rn(32768, 4096), rn(4096, 14336, scale=0.02)
+        fn = lambda: nt.mm(a, b)  # noqa: E731
+    elif name == "addmm_c5":  # BASELINE config 5 addmm
+        a, b, c = rn(16384, 8192), rn(8192, 8192, scale=0.02), rn(8192)
+        fn = lambda: nt.addmm(c, a, b)  # noqa: E731
+    elif name == "sdpa_causal":  # a quarter-size slice of config 5 attention (B2 H32 S4096 D128)
+        q, k, v = rn(2, 32, 4096, 128), rn(2, 32, 4096, 128), rn(2, 32, 4096, 128)
+        fn = lambda: nt.scaled_dot_product_attention(q, k, v, is_causal=True)  # noqa: E731
+    elif name == "sdpa":
+        q, k, v = rn(2, 32, 4096, 128), rn(2, 32, 4096, 128), rn(2, 32, 4096, 128)
+        fn = lambda: nt.scaled_dot_product_attention(q, k, v)  # noqa: E731
+    elif name == "softmax_c4":
+        x = rn(4096, 32768, dt=torch.float32, scale=2.0)
+        fn = lambda: nt.softmax(x, -1)  # noqa: E731
+    elif name == "layer_norm_c4":
+        x, w, b = rn(32768, 8192), rn(8192), rn(8192)
+        fn = lambda: nt.layer_norm(x, (8192,), w, b, 1e-5)  # noqa: E731
+    elif name == "rms_norm_c1":
+        x, w = rn(8, 512, 4096, dt=torch.float32), rn(4096, dt=torch.float32)
+        fn = lambda: nt.rms_norm(x, (4096,), w, 1e-6)  # noqa: E731
+    elif name == "silu_bf16":
+        x = rn(1 << 28)
+        fn = lambda: nt.silu(x)  # noqa: E731
+    elif name == "rope_q":
+        from ntops_b200.chain import rope_tables
+
+        x = rn(16, 2048, 32, 128)
+        sn, cs = rope_tables(2048, dev)
+        fn = lambda: nt.rotary_position_embedding(x, sn, cs, interleaved=False)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown case {name}")
+    print(json.dumps({"case": name, "ms": time_op(fn, iters=reps, warmup=1)}), flush=True)
+
+
 # ---------------------------------------------------------------------------- main --------
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
@@ -305,7 +353,11 @@ def main():
     ap.add_argument("--impl", default="ntops_b200", choices=["ntops_b200", "reference"])
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op table")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--case", default=None, help="run one operator case (for ncu) and exit")
+    ap.add_argument("--reps", type=int, default=2)
     args = ap.parse_args()
+    if args.case:
+        return run_case(args.case, args.reps)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

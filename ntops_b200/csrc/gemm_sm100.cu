@@ -298,8 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // --------------------------------------------------------------- CUDA-core fallback ------
 // 64 x 64 output tile per 256-thread block, 4 x 4 outputs per thread, K staged through shared
-// memory 16 at a time; accumulates in Acc (fp32, or fp64 for fp64 operands).  Handles any
-// strides, K = 0, IEEE fp32 and fp64.
+// memory 16 at a time; accumulates in Acc (fp32 for 16-bit operands, fp64 for fp32 / fp64).
+// Handles any strides, K = 0, IEEE fp32 and fp64.
 struct SimtArgs {
   const void* a;
   const void* b;
@@ -415,7 +415,10 @@ int launch_simt(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand
   s.b_ks = ob.s_k;
   dim3 grid((p.N + 63) / 64, (p.M + 63) / 64, p.batch);
   NTB_UNSUP(grid.y <= 65535 && grid.z <= 65535, "problem too large for the CUDA-core GEMM");
-  using Acc = typename std::conditional<std::is_same<T, double>::value, double, float>::type;
+  // IEEE fp32 ("highest" precision) and fp64 accumulate in fp64: products of fp32 values are
+  // exact in fp64, so the result is the correctly rounded sum up to fp64 summation error.
+  using Acc = typename std::conditional<std::is_same<T, double>::value || std::is_same<T, float>::value, double,
+                                        float>::type;
   gemm_simt_kernel<T, Acc><<<grid, 256, 0, st>>>(s, p);
   NTB_LAUNCH_CHECK();
   return NTB_OK;
