@@ -44,6 +44,9 @@ UNIT = "tokens/s"
 GLOBAL_BATCH = 16
 SEQ = 2048
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) of one launch of the fused gate/up (SwiGLU) projection at the full
+# chain size, from the ncu capture summarised in profiles/ (None until captured).
+SWIGLU_GEMM_TRAFFIC = None
 
 
 def load_peaks():
@@ -64,12 +67,13 @@ def config(world):
         "seq_len": SEQ,
         "parallelism": f"dp{world} (sequences sharded, no data-path collective)",
         "l2": "inputs larger than L2 (x 268 MB + weights 436 MB per pass)",
+        "fusions": "gate/up projections + silu*mul as one tcgen05 GEMM with a SwiGLU epilogue",
     }
 
 
 # ------------------------------------------------------------------------- clocks ---------
 class ClockSampler:
-    """Samples SM clock and clock-event reasons with NVML every 100 ms (read-only)."""
+    """Samples SM clock and clock-event reasons with NVML every 20 ms (read-only)."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
@@ -102,7 +106,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.1)
+            self._stop.wait(0.02)
 
     def __enter__(self):
         if self._nv is not None:
@@ -191,10 +195,14 @@ def run_reference(args, rank, world):
 
 # ---------------------------------------------------------------------- per-op table ------
 def time_op(fn, iters=10, warmup=3, flush=None):
-    """Median CUDA-event time (ms) of fn(); `flush` (writing > L2) runs between iterations."""
+    """Median CUDA-event time (ms) of fn(); `flush` (writing > L2) runs between iterations.
+
+    All iterations are enqueued before one synchronisation, so the host runs ahead of the GPU
+    and each event pair brackets device time only (no launch latency of an idle GPU)."""
     for _ in range(warmup):
         fn()
-    times = []
+    torch.cuda.synchronize()
+    pairs = []
     for _ in range(iters):
         if flush is not None:
             flush()
@@ -202,9 +210,9 @@ def time_op(fn, iters=10, warmup=3, flush=None):
         s.record()
         fn()
         e.record()
-        e.synchronize()
-        times.append(s.elapsed_time(e))
-    return statistics.median(times)
+        pairs.append((s, e))
+    torch.cuda.synchronize()
+    return statistics.median(s.elapsed_time(e) for s, e in pairs)
 
 
 def per_op_table(dev, peaks):
@@ -293,6 +301,13 @@ def per_op_table(dev, peaks):
     tf("sdpa_bf16_8x32x8192x128", lambda: nt.scaled_dot_product_attention(qa, ka, va), fl)
     tf("sdpa_causal_bf16_8x32x8192x128", lambda: nt.scaled_dot_product_attention(qa, ka, va, is_causal=True),
        fl * (8192 + 1) / (2 * 8192))
+    del qa, ka, va
+    # decode step against an 8192-token KV cache (Llama-3-8B heads): HBM-bound on K / V
+    qd = torch.randn(8, 32, 1, 128, generator=g, device=dev).to(torch.bfloat16)
+    kd = torch.randn(8, 8, 8192, 128, generator=g, device=dev).to(torch.bfloat16)
+    vd = torch.randn(8, 8, 8192, 128, generator=g, device=dev).to(torch.bfloat16)
+    bw("sdpa_decode_bf16_b8_hq32_hkv8_kv8192", lambda: nt.scaled_dot_product_attention(qd, kd, vd, enable_gqa=True),
+       (kd.numel() + vd.numel()) * 2 + 2 * qd.numel() * 2, use_flush=True)
     return res
 
 
@@ -312,6 +327,11 @@ def run_case(name, reps):
     if name == "gemm_gate":  # chain gate projection: [32768, 4096] x [4096, 14336]
         a, b = rn(32768, 4096), rn(4096, 14336, scale=0.02)
         fn = lambda: nt.mm(a, b)  # noqa: E731
+    elif name == "swiglu":  # chain fused gate/up projection: [32768, 4096] x [4096, 2 x 14336]
+        from ntops_b200.fused import swiglu_linear
+
+        a, b = rn(32768, 4096), rn(4096, 2 * 14336, scale=0.02)
+        fn = lambda: swiglu_linear(a, b)  # noqa: E731
     elif name == "addmm_c5":  # BASELINE config 5 addmm
         a, b, c = rn(16384, 8192), rn(8192, 8192, scale=0.02), rn(8192)
         fn = lambda: nt.addmm(c, a, b)  # noqa: E731
@@ -330,6 +350,9 @@ def run_case(name, reps):
     elif name == "rms_norm_c1":
         x, w = rn(8, 512, 4096, dt=torch.float32), rn(4096, dt=torch.float32)
         fn = lambda: nt.rms_norm(x, (4096,), w, 1e-6)  # noqa: E731
+    elif name == "sdpa_decode":
+        q, k, v = rn(8, 32, 1, 128), rn(8, 8, 8192, 128), rn(8, 8, 8192, 128)
+        fn = lambda: nt.scaled_dot_product_attention(q, k, v, enable_gqa=True)  # noqa: E731
     elif name == "silu_bf16":
         x = rn(1 << 28)
         fn = lambda: nt.silu(x)  # noqa: E731
@@ -415,7 +438,13 @@ def main():
         torch.cuda.synchronize()
     launches = ntu.launch_count - launches0
     ms_local = start.elapsed_time(end)
-    gemm_ms = sum(s.elapsed_time(e) for s, e in gemm_events)
+    gemm_times = [s.elapsed_time(e) for s, e in gemm_events]
+    gemm_ms = sum(gemm_times)
+    # the fused gate/up (SwiGLU) projection is the 5th of the 6 launches of a pass
+    shapes = chain.gemm_shapes(tokens)
+    gate_ms = statistics.mean(gemm_times[4::len(shapes)])
+    gm, gn, gk = shapes[4]
+    gate_tflops = 2 * gm * gn * gk / (gate_ms * 1e-3) / 1e12
     ms = max_over_ranks(ms_local, dev)
     value = GLOBAL_BATCH * SEQ * args.steps / (ms * 1e-3)
     gemm_tflops = mm_flops * args.steps / (gemm_ms * 1e-3) / 1e12
@@ -424,31 +453,61 @@ def main():
     checksum = float(y.float().abs().mean())
     assert checksum == checksum and checksum > 0, "non-finite layer output"
 
-    # ---- end to end: pinned host input in, output back, every step
+    # ---- end to end: every step's input comes from pinned host memory and its output goes
+    # back to pinned host memory, through the public API.  The copies run on their own streams
+    # (double-buffered), so step i+1's upload and step i-1's download overlap step i's kernels.
     xh = x.cpu().pin_memory()
-    yh = torch.empty(y.shape, dtype=y.dtype).pin_memory()
-    xd = torch.empty_like(x)
-    for _ in range(2):
-        xd.copy_(xh, non_blocking=True)
-        yh.copy_(chain.layer_forward(xd, wts, sin, cos), non_blocking=True)
+    yh = [torch.empty(y.shape, dtype=y.dtype).pin_memory() for _ in range(2)]
+    xbuf = [torch.empty_like(x) for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    x_free = [ev(), ev()]
+    y_free = [ev(), ev()]
+    for i in range(2):
+        x_free[i].record(comp)
+        y_free[i].record(down)
+
+    def e2e_steps(n):
+        for i in range(n):
+            b = i & 1
+            with torch.cuda.stream(up):
+                up.wait_event(x_free[b])
+                xbuf[b].copy_(xh, non_blocking=True)
+                x_ready = ev()
+                x_ready.record(up)
+            comp.wait_event(x_ready)
+            out = chain.layer_forward(xbuf[b], wts, sin, cos)
+            x_free[b].record(comp)
+            out_ready = ev()
+            out_ready.record(comp)
+            with torch.cuda.stream(down):
+                down.wait_event(out_ready)
+                down.wait_event(y_free[b])
+                yh[b].copy_(out, non_blocking=True)
+                out.record_stream(down)
+                y_free[b].record(down)
+        comp.wait_stream(up)
+        comp.wait_stream(down)
+
+    e2e_steps(2)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(args.steps):
-        xd.copy_(xh, non_blocking=True)
-        yh.copy_(chain.layer_forward(xd, wts, sin, cos), non_blocking=True)
-    e2.record()
+    s2.record(comp)
+    e2e_steps(args.steps)
+    e2.record(comp)
     torch.cuda.synchronize()
     ms_e2e = max_over_ranks(s2.elapsed_time(e2), dev)
     e2e_value = GLOBAL_BATCH * SEQ * args.steps / (ms_e2e * 1e-3)
+    assert torch.equal(yh[(args.steps - 1) & 1], y.cpu()), "end-to-end output differs from the resident run"
 
     ops = None
     cpu = None
     if world == 1 and rank == 0:
         if not args.no_ops:
-            del xd
+            del xbuf, yh
             ops = per_op_table(dev, peaks)
         if not args.no_cpu:
             ctoks = pick_cpu_tokens()
@@ -475,11 +534,18 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": x.numel() * 2 * world,
                     "d2h_bytes_per_step": y.numel() * 2 * world},
             "gpu_launches": launches * world,
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, 7 projections per step)",
-                         "achieved": gemm_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                         "frac": gemm_tflops / peaks["bf16_tflops_sustained"], "traffic": None,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (SwiGLU epilogue)",
+                         "launch": f"fused gate/up projection [{gm}x{gk}]x[{gk}x{gn}] bf16 -> [{gm}x{gn // 2}] "
+                                   "(largest of the 6 per step)",
+                         "achieved": gate_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                         "frac": gate_tflops / peaks["bf16_tflops_sustained"],
+                         "traffic": SWIGLU_GEMM_TRAFFIC if batch == GLOBAL_BATCH else None,
+                         "traffic_algorithmic": (gm * gk + gk * gn + gm * gn // 2) * 2,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
+                                           "shape (profiles/gemm_tc_kernel-swiglu_32768x28672x4096_bf16.md)",
                          "peak_source": f"bf16_tflops_sustained, {peak_src}",
-                         "gemm_share_of_step": gemm_ms / ms_local},
+                         "all_gemms": {"achieved": gemm_tflops, "frac": gemm_tflops / peaks["bf16_tflops_sustained"],
+                                       "share_of_step": gemm_ms / ms_local}},
             "step_tflops": (mm_flops + attn_flops) * GLOBAL_BATCH / batch / (ms / args.steps * 1e-3) / 1e12,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,

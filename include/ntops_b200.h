@@ -95,7 +95,10 @@ typedef enum {
   NTB_UN_ISNAN = 13,      /* torch/isnan.py:7-11,      kernels/isnan.py:8  (bool out) */
   NTB_UN_ISINF = 14,      /* torch/isinf.py:7-11,      kernels/isinf.py:8-11 (bool out) */
   NTB_UN_BITWISE_NOT = 15,/* torch/bitwise_not.py:7-17, kernels/bitwise_not.py:9-24 */
-  NTB_UN_CLAMP = 16       /* torch/clamp.py:7-15 with scalar bounds, kernels/clamp.py:9-10 */
+  NTB_UN_CLAMP = 16,      /* torch/clamp.py:7-15 with scalar bounds, kernels/clamp.py:9-10 */
+  NTB_UN_RAD2DEG = 17,    /* torch/rad2deg.py:37, kernels/rad2deg.py:13-19: x * 180 / pi */
+  NTB_UN_FRAC = 18,       /* torch/frac.py (frac), kernels/frac.py:12-27: x - trunc(x) */
+  NTB_UN_LGAMMA = 19      /* torch/lgamma.py:11, kernels/lgamma.py:14-29: log|gamma(x)| */
 } NtbUnaryOp;
 
 /* y = op(x).  x and y have the same shape (x may carry 0 strides).  scalars: NTB_UN_CLAMP
@@ -120,7 +123,10 @@ typedef enum {
   NTB_BIN_GT = 11,         /* torch/gt.py:7,     kernels/gt.py:8-9                         */
   NTB_BIN_GE = 12,         /* torch/ge.py:7,     kernels/ge.py:8-9                         */
   NTB_BIN_BITWISE_AND = 13,/* torch/bitwise_and.py:7-15, kernels/bitwise_and.py:8-9       */
-  NTB_BIN_BITWISE_OR = 14  /* torch/bitwise_or.py:7-15,  kernels/bitwise_or.py:8-9        */
+  NTB_BIN_BITWISE_OR = 14, /* torch/bitwise_or.py:7-15,  kernels/bitwise_or.py:8-9        */
+  NTB_BIN_COPYSIGN = 15,   /* torch/copysign.py:33, kernels/copysign.py:13-53 (|a| with b's sign) */
+  NTB_BIN_NEXTAFTER = 16,  /* torch/nextafter.py:36, kernels/nextafter.py:13-123 (next float toward b) */
+  NTB_BIN_LCM = 17         /* torch/lcm.py:4-92, kernels/lcm.py:14-128 (integers) */
 } NtbBinaryOp;
 
 /* y = op(a, b).  a, b and y share y's shape (inputs may carry 0 strides for broadcasting);
@@ -181,6 +187,14 @@ NTB_API int ntb_rotary_position_embedding(const NtbTensor* x, const NtbTensor* s
 NTB_API int ntb_gemm(const NtbTensor* a, const NtbTensor* bm, const NtbTensor* c, const NtbTensor* d,
              double alpha, double beta, int precision, void* stream);
 
+/* Fused SwiGLU projection of the Llama MLP: d = silu(a @ Wg) * (a @ Wu) in one tcgen05 GEMM.
+ * a: [M, K]; w: [K, 2N] holding Wg and Wu interleaved in column blocks of 128
+ * (w[:, 256*i : 256*i+128] = Wg[:, 128*i : 128*i+128], w[:, 256*i+128 : 256*(i+1)] = Wu[...]);
+ * d: [M, N].  bf16 or fp16; N a multiple of 128.  The gate / up products never reach HBM.
+ * No single reference entry: it fuses the chain steps mm (torch/mm.py:7-18) x 2, silu
+ * (torch/silu.py:7-17) and mul (torch/mul.py:7-15). */
+NTB_API int ntb_gemm_swiglu(const NtbTensor* a, const NtbTensor* w, const NtbTensor* d, void* stream);
+
 /* -------------------------------------------------------------- attention ---------------- */
 
 /* Causal variants (kernels/scaled_dot_product_attention.py:12-17): 0 = none. */
@@ -196,6 +210,19 @@ NTB_API int ntb_gemm(const NtbTensor* a, const NtbTensor* bm, const NtbTensor* c
  * kernels/scaled_dot_product_attention.py:154-201. */
 NTB_API int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
              const NtbTensor* o, double scale, int causal_variant, void* stream);
+
+/* Attention for short query blocks (GQA group x Sq <= 64 rows per kv head, e.g. decoding
+ * against a KV cache) split over the key range for parallelism.  Same tensors and semantics as
+ * ntb_sdpa (fp16 / bf16 / fp32, head_dim <= 256, optional additive mask, causal variants);
+ * `workspace` is caller-allocated device memory of at least ntb_sdpa_decode_workspace() bytes
+ * (16-byte aligned) holding each key chunk's partial output, max and sum.
+ * Replaces the KV-cache path of torch/scaled_dot_product_attention.py:79-94 +
+ * kernels/scaled_dot_product_attention.py:123-151. */
+NTB_API int ntb_sdpa_decode_workspace(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v,
+                                      int64_t* bytes);
+NTB_API int ntb_sdpa_decode(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+                            const NtbTensor* o, double scale, int causal_variant, void* workspace,
+                            int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

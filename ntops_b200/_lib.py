@@ -32,11 +32,12 @@ DTYPE_CODES = {
 UNARY = {
     "copy": 0, "neg": 1, "abs": 2, "relu": 3, "exp": 4, "sigmoid": 5, "silu": 6, "gelu": 7,
     "gelu_tanh": 8, "tanh": 9, "rsqrt": 10, "sin": 11, "cos": 12, "isnan": 13, "isinf": 14,
-    "bitwise_not": 15, "clamp": 16,
+    "bitwise_not": 15, "clamp": 16, "rad2deg": 17, "frac": 18, "lgamma": 19,
 }
 BINARY = {
     "add": 0, "sub": 1, "mul": 2, "div": 3, "div_trunc": 4, "div_floor": 5, "pow": 6,
     "eq": 7, "ne": 8, "lt": 9, "le": 10, "gt": 11, "ge": 12, "bitwise_and": 13, "bitwise_or": 14,
+    "copysign": 15, "nextafter": 16, "lcm": 17,
 }
 
 PRECISION_TF32, PRECISION_IEEE = 1, 2
@@ -55,7 +56,10 @@ EXPORTS = (
     "ntb_softmax",
     "ntb_rotary_position_embedding",
     "ntb_gemm",
+    "ntb_gemm_swiglu",
     "ntb_sdpa",
+    "ntb_sdpa_decode_workspace",
+    "ntb_sdpa_decode",
 )
 
 
@@ -89,7 +93,13 @@ _SIGNATURES = {
         [_P, _P, _P, _P, ctypes.c_double, ctypes.c_double, ctypes.c_int, _VP],
         ctypes.c_int,
     ),
+    "ntb_gemm_swiglu": ([_P, _P, _P, _VP], ctypes.c_int),
     "ntb_sdpa": ([_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP], ctypes.c_int),
+    "ntb_sdpa_decode_workspace": ([_P, _P, _P, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
+    "ntb_sdpa_decode": (
+        [_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP, ctypes.c_int64, _VP],
+        ctypes.c_int,
+    ),
 }
 
 _lib = None

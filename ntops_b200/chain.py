@@ -43,6 +43,9 @@ class LayerWeights:
         self.wd = w(FFN, HIDDEN)
         self.norm1 = torch.ones(HIDDEN, device=device, dtype=dtype)
         self.norm2 = torch.ones(HIDDEN, device=device, dtype=dtype)
+        from ntops_b200.fused import pack_swiglu_weight
+
+        self.wgu = pack_swiglu_weight(self.wg, self.wu)  # for the fused SwiGLU projection
 
     def tensors(self):
         return [self.wq, self.wk, self.wv, self.wo, self.wg, self.wu, self.wd, self.norm1, self.norm2]
@@ -55,17 +58,17 @@ def rope_tables(seq_len, device, dtype=torch.bfloat16):
     return torch.sin(pos * inv).to(dtype).to(device), torch.cos(pos * inv).to(dtype).to(device)
 
 
-def gemm_shapes(tokens):
-    """(M, N, K) of the seven projections of one layer pass."""
-    return [
+def gemm_shapes(tokens, fused=True):
+    """(M, N, K) of the projection launches of one layer pass, in launch order (with ``fused``
+    the gate and up projections are one launch of width 2 * FFN)."""
+    head = [
         (tokens, HEADS * HEAD_DIM, HIDDEN),
         (tokens, KV_HEADS * HEAD_DIM, HIDDEN),
         (tokens, KV_HEADS * HEAD_DIM, HIDDEN),
         (tokens, HIDDEN, HEADS * HEAD_DIM),
-        (tokens, FFN, HIDDEN),
-        (tokens, FFN, HIDDEN),
-        (tokens, HIDDEN, FFN),
     ]
+    mlp = [(tokens, 2 * FFN, HIDDEN)] if fused else [(tokens, FFN, HIDDEN), (tokens, FFN, HIDDEN)]
+    return head + mlp + [(tokens, HIDDEN, FFN)]
 
 
 def layer_flops(batch, seq):
@@ -77,14 +80,19 @@ def layer_flops(batch, seq):
     return mm, attn
 
 
-def layer_forward(x, wts, sin, cos, mm_hook=None):
+def layer_forward(x, wts, sin, cos, mm_hook=None, fused=True):
     """One pass of the op chain on x [B, S, 4096] (bf16); returns the down projection [B, S, 4096].
 
-    ``mm_hook(fn)``, when given, wraps every projection call (the benchmark uses it to time the
-    GEMMs with CUDA events)."""
+    ``fused`` computes gate / up / silu / mul as one GEMM with a SwiGLU epilogue
+    (``ntops_b200.fused.swiglu_linear``); otherwise each step is its own operator.
+    ``mm_hook(fn, a, b)``, when given, wraps every projection call (the benchmark times the
+    GEMMs with CUDA events through it)."""
+    from ntops_b200 import fused as F
+
     B, S, _ = x.shape
     T = B * S
     mm = nt.mm if mm_hook is None else (lambda a, b: mm_hook(nt.mm, a, b))
+    swiglu = F.swiglu_linear if mm_hook is None else (lambda a, b: mm_hook(F.swiglu_linear, a, b))
     x2 = x.view(T, HIDDEN)
     h = nt.rms_norm(x2, (HIDDEN,), wts.norm1, EPS)
     q = mm(h, wts.wq).view(B, S, HEADS, HEAD_DIM)
@@ -98,8 +106,11 @@ def layer_forward(x, wts, sin, cos, mm_hook=None):
     attn = mm(o2, wts.wo)
     x2 = nt.add(x2, attn)
     h2 = nt.rms_norm(x2, (HIDDEN,), wts.norm2, EPS)
-    gate = mm(h2, wts.wg)
-    up = mm(h2, wts.wu)
-    act = nt.mul(nt.silu(gate), up)
+    if fused:
+        act = swiglu(h2, wts.wgu)
+    else:
+        gate = mm(h2, wts.wg)
+        up = mm(h2, wts.wu)
+        act = nt.mul(nt.silu(gate), up)
     down = mm(act, wts.wd)
     return down.view(B, S, HIDDEN)

@@ -2,7 +2,9 @@
 // bounded in-kernel waits set, and the tensor checks shared by every entry point.
 #include <cstdarg>
 #include <cstdio>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "ntb_common.cuh"
 
@@ -91,6 +93,42 @@ int sm_count() {
   }
   return cache[dev];
 }
+
+namespace rr {
+int blocks_per_sm(const void* kernel, int bt) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(kernel, bt);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, bt, 0) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = 1;
+  }
+  cache[key] = n;
+  return n;
+}
+}  // namespace rr
+
+namespace rs {
+int blocks_per_sm_smem(const void* kernel, int bt, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, std::pair<int, size_t>>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(kernel, std::make_pair(bt, smem));
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, bt, smem) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = 1;
+  }
+  cache[key] = n;
+  return n;
+}
+}  // namespace rs
 
 int check_tensor(const NtbTensor* t, const char* name) {
   NTB_ARG(t != nullptr, "%s: tensor descriptor is NULL", name);

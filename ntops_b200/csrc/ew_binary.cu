@@ -86,7 +86,14 @@ extern "C" int ntb_binary(int op, const NtbTensor* a, const NtbTensor* b, const 
     case NTB_BIN_DIV: return run_arith(ops::Div{}, a, b, y, st, false);
     case NTB_BIN_DIV_TRUNC: return run_arith(ops::DivTrunc{}, a, b, y, st, true);
     case NTB_BIN_DIV_FLOOR: return run_arith(ops::DivFloor{}, a, b, y, st, true);
-    case NTB_BIN_POW: return run_arith(ops::Pow{}, a, b, y, st, true);
+    case NTB_BIN_POW:
+      if (a->dtype == NTB_F16 || a->dtype == NTB_BF16) {
+        const NtbTensor* xs[2] = {a, b};
+        NTB_UNSUP(y->dtype == a->dtype, "output dtype must equal input dtype");
+        if (a->dtype == NTB_F16) return ew::launch<2, __half, __half>(ops::PowFast{}, xs, y, st);
+        return ew::launch<2, __nv_bfloat16, __nv_bfloat16>(ops::PowFast{}, xs, y, st);
+      }
+      return run_arith(ops::Pow{}, a, b, y, st, true);
     case NTB_BIN_EQ: return run_compare(ops::Eq{}, a, b, y, st);
     case NTB_BIN_NE: return run_compare(ops::Ne{}, a, b, y, st);
     case NTB_BIN_LT: return run_compare(ops::Lt{}, a, b, y, st);
@@ -95,6 +102,24 @@ extern "C" int ntb_binary(int op, const NtbTensor* a, const NtbTensor* b, const 
     case NTB_BIN_GE: return run_compare(ops::Ge{}, a, b, y, st);
     case NTB_BIN_BITWISE_AND: return run_bitwise(ops::BitAnd{}, a, b, y, st);
     case NTB_BIN_BITWISE_OR: return run_bitwise(ops::BitOr{}, a, b, y, st);
+    case NTB_BIN_COPYSIGN: return run_arith(ops::CopySign{}, a, b, y, st, false);
+    case NTB_BIN_NEXTAFTER: {
+      const NtbTensor* xs[2] = {a, b};
+      NTB_UNSUP(y->dtype == a->dtype, "output dtype must equal input dtype");
+      if (a->dtype == NTB_F16) return ew::launch<2, __half, __half>(ops::NextAfter16<__half>{}, xs, y, st);
+      if (a->dtype == NTB_BF16)
+        return ew::launch<2, __nv_bfloat16, __nv_bfloat16>(ops::NextAfter16<__nv_bfloat16>{}, xs, y, st);
+      if (a->dtype == NTB_F32) return ew::launch<2, float, float>(ops::NextAfter{}, xs, y, st);
+      if (a->dtype == NTB_F64) return ew::launch<2, double, double>(ops::NextAfter{}, xs, y, st);
+      set_error("nextafter needs a floating dtype");
+      return NTB_ERR_UNSUPPORTED;
+    }
+    case NTB_BIN_LCM: {
+      const NtbTensor* xs[2] = {a, b};
+      NTB_UNSUP(y->dtype == a->dtype, "output dtype must equal input dtype");
+      NTB_DISPATCH_INT(a->dtype, return (ew::launch<2, scalar_t, scalar_t>(ops::Lcm{}, xs, y, st)));
+      return NTB_OK;
+    }
     default: set_error("unknown binary op code %d", op); return NTB_ERR_INVALID;
   }
 }

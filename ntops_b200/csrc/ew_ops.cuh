@@ -2,7 +2,9 @@
 // double, the integer type itself for integers) and follows the CUDA semantics that PyTorch
 // gives the same operator, which is the oracle the reference's tests compare against
 // (tests/test_<op>.py in the ntops project).  Transcendentals call CUDA's accurate math
-// functions (expf, erff, tanhf, powf, sinf, cosf, sqrtf), never the __ intrinsics.
+// functions (expf, erff, tanhf, powf, sinf, cosf, sqrtf) for fp32 / fp64 outputs; fp16 / bf16
+// outputs of exp, sigmoid, silu, gelu-tanh, tanh, rsqrt and pow use the hardware
+// approximations of the "fast forms" section, whose error is far below the output rounding.
 #pragma once
 
 #include <math.h>
@@ -103,6 +105,73 @@ struct ClampScalar {
   }
 };
 
+struct Rad2Deg {
+  template <typename T> __device__ T operator()(T x) const { return x * T(57.295779513082320876798154814105); }
+};
+struct Frac {
+  template <typename T> __device__ T operator()(T x) const { return x - m_trunc(x); }
+};
+struct Lgamma {
+  __device__ float operator()(float x) const { return lgammaf(x); }
+  __device__ double operator()(double x) const { return lgamma(x); }
+};
+
+// ------------------------------------------------- fast forms for 16-bit outputs ----------
+// Used only when the result is rounded to fp16 / bf16: the hardware approximations below
+// (ex2 / lg2 / rcp / rsqrt ~2^-22 relative error, tanh.approx ~2^-11) are well inside the
+// 2^-11 / 2^-8 rounding of those outputs, and they keep the kernels memory-bound.
+__device__ __forceinline__ float hw_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float hw_lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float hw_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float hw_tanh(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float hw_rsqrt(float x) {
+  float y;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct ExpFast { __device__ float operator()(float x) const { return hw_ex2(x * kLog2e); } };
+struct SigmoidFast { __device__ float operator()(float x) const { return hw_rcp(1.f + hw_ex2(-x * kLog2e)); } };
+struct SiluFast { __device__ float operator()(float x) const { return x * hw_rcp(1.f + hw_ex2(-x * kLog2e)); } };
+struct GeluTanhFast {
+  __device__ float operator()(float x) const {
+    const float inner = 0.79788456080286535588f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.f + hw_tanh(inner));
+  }
+};
+struct TanhFast { __device__ float operator()(float x) const { return hw_tanh(x); } };
+struct RsqrtFast { __device__ float operator()(float x) const { return hw_rsqrt(x); } };
+// x^e = 2^(e * log2|x|) with the sign of an odd integer exponent; NaN for a negative base with a
+// fractional exponent; pow(x, 0) = pow(1, e) = 1 (C / torch semantics).
+struct PowFast {
+  __device__ float operator()(float a, float b) const {
+    if (b == 0.f || a == 1.f) return 1.f;
+    float r = hw_ex2(b * hw_lg2(fabsf(a)));
+    if (a < 0.f) {
+      if (b != truncf(b)) return __int_as_float(0x7fffffff);
+      if (fabsf(b) < 16777216.f && (((int)b) & 1)) r = -r;
+    }
+    return r;
+  }
+};
+
 // ----------------------------------------------------------------------- binary -----------
 template <typename M>
 struct Add {
@@ -192,6 +261,56 @@ struct BitAnd {
 struct BitOr {
   template <typename T> __device__ T operator()(T a, T b) const { return T(a | b); }
   __device__ bool operator()(bool a, bool b) const { return a || b; }
+};
+
+struct CopySign {
+  __device__ float operator()(float a, float b) const { return copysignf(a, b); }
+  __device__ double operator()(double a, double b) const { return copysign(a, b); }
+  // integer operands are promoted to floating point by the caller; never instantiated at run time
+  template <typename T> __device__ T operator()(T a, T) const { return a; }
+};
+// The representable value after `a` in the direction of `b` in the 16-bit storage type T
+// (one step of the IEEE encoding): b when a == b, NaN when either is NaN, the smallest
+// subnormal with b's sign from +-0.  Values arrive as the exact float images of T values.
+template <typename T>
+struct NextAfter16 {
+  __device__ float operator()(float fa, float fb) const {
+    if (fa != fa || fb != fb) return fa + fb;
+    if (fa == fb) return fb;
+    const T ta = cvt<T>(fa), tb = cvt<T>(fb);
+    const uint16_t ua = *reinterpret_cast<const uint16_t*>(&ta);
+    const uint16_t ub = *reinterpret_cast<const uint16_t*>(&tb);
+    uint16_t r;
+    if ((ua & 0x7fffu) == 0) {
+      r = (uint16_t)((ub & 0x8000u) | 1u);
+    } else if ((fa < fb) == !(ua & 0x8000u)) {
+      r = (uint16_t)(ua + 1u);  // away from zero
+    } else {
+      r = (uint16_t)(ua - 1u);  // toward zero
+    }
+    return cvt<float>(*reinterpret_cast<const T*>(&r));
+  }
+};
+struct NextAfter {
+  __device__ float operator()(float a, float b) const { return nextafterf(a, b); }
+  __device__ double operator()(double a, double b) const { return nextafter(a, b); }
+};
+// lcm(a, b) = |a / gcd(a, b) * b| (0 when either is 0), gcd by Euclid's algorithm.  The
+// product and its absolute value are taken in the C++-promoted type (int for 8/16-bit inputs)
+// before narrowing, which is how torch's lcm treats a result that overflows the input type.
+struct Lcm {
+  template <typename T> __device__ T operator()(T a, T b) const {
+    using P = decltype(+a);
+    if (a == T(0) || b == T(0)) return T(0);
+    P x = a < T(0) ? -P(a) : P(a), y = b < T(0) ? -P(b) : P(b);
+    while (y != P(0)) {
+      const P t = x % y;
+      x = y;
+      y = t;
+    }
+    P r = P(a) / x * P(b);
+    return T(r < P(0) ? -r : r);
+  }
 };
 
 // ---------------------------------------------------------------------- ternary -----------

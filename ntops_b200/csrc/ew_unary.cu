@@ -19,6 +19,17 @@ int run_float(const Op& op, const NtbTensor* x, const NtbTensor* y, cudaStream_t
   return NTB_OK;
 }
 
+// Accurate functor for fp32 / fp64 outputs, fast functor (fp32 math) for fp16 / bf16 outputs.
+template <typename Op, typename Fast>
+int run_float2(const Op& op, const Fast& fast, const NtbTensor* x, const NtbTensor* y, cudaStream_t st) {
+  NTB_UNSUP(x->dtype == y->dtype, "output dtype %s must equal input dtype %s", dtype_name(y->dtype),
+            dtype_name(x->dtype));
+  const NtbTensor* xs[1] = {x};
+  if (x->dtype == NTB_F16) return ew::launch<1, __half, __half>(fast, xs, y, st);
+  if (x->dtype == NTB_BF16) return ew::launch<1, __nv_bfloat16, __nv_bfloat16>(fast, xs, y, st);
+  return run_float(op, x, y, st);
+}
+
 template <typename Op>
 int run_signed(const Op& op, const NtbTensor* x, const NtbTensor* y, cudaStream_t st) {
   NTB_UNSUP(x->dtype == y->dtype, "output dtype %s must equal input dtype %s", dtype_name(y->dtype),
@@ -83,19 +94,22 @@ extern "C" int ntb_unary(int op, const NtbTensor* x, const NtbTensor* y, const d
     case NTB_UN_NEG: return run_signed(ops::Neg{}, x, y, st);
     case NTB_UN_ABS: return run_signed(ops::Abs{}, x, y, st);
     case NTB_UN_RELU: return run_signed(ops::Relu{}, x, y, st);
-    case NTB_UN_EXP: return run_float(ops::Exp{}, x, y, st);
-    case NTB_UN_SIGMOID: return run_float(ops::Sigmoid{}, x, y, st);
-    case NTB_UN_SILU: return run_float(ops::Silu{}, x, y, st);
+    case NTB_UN_EXP: return run_float2(ops::Exp{}, ops::ExpFast{}, x, y, st);
+    case NTB_UN_SIGMOID: return run_float2(ops::Sigmoid{}, ops::SigmoidFast{}, x, y, st);
+    case NTB_UN_SILU: return run_float2(ops::Silu{}, ops::SiluFast{}, x, y, st);
     case NTB_UN_GELU: return run_float(ops::Gelu{}, x, y, st);
-    case NTB_UN_GELU_TANH: return run_float(ops::GeluTanh{}, x, y, st);
-    case NTB_UN_TANH: return run_float(ops::Tanh{}, x, y, st);
-    case NTB_UN_RSQRT: return run_float(ops::Rsqrt{}, x, y, st);
+    case NTB_UN_GELU_TANH: return run_float2(ops::GeluTanh{}, ops::GeluTanhFast{}, x, y, st);
+    case NTB_UN_TANH: return run_float2(ops::Tanh{}, ops::TanhFast{}, x, y, st);
+    case NTB_UN_RSQRT: return run_float2(ops::Rsqrt{}, ops::RsqrtFast{}, x, y, st);
     case NTB_UN_SIN: return run_float(ops::Sin{}, x, y, st);
     case NTB_UN_COS: return run_float(ops::Cos{}, x, y, st);
     case NTB_UN_ISNAN: return run_to_bool(ops::IsNan{}, x, y, st);
     case NTB_UN_ISINF: return run_to_bool(ops::IsInf{}, x, y, st);
     case NTB_UN_BITWISE_NOT: return run_bitwise_not(x, y, st);
     case NTB_UN_CLAMP: return run_clamp(x, y, scalars, num_scalars, st);
+    case NTB_UN_RAD2DEG: return run_float(ops::Rad2Deg{}, x, y, st);
+    case NTB_UN_FRAC: return run_float(ops::Frac{}, x, y, st);
+    case NTB_UN_LGAMMA: return run_float(ops::Lgamma{}, x, y, st);
     default: set_error("unknown unary op code %d", op); return NTB_ERR_INVALID;
   }
 }

@@ -7,7 +7,8 @@
 // acc / l.  The reference does not skip KV blocks above the causal diagonal.
 //
 // sm_100a kernel (bf16 / fp16, head_dim 64 or 128, no additive mask):
-//   * one CTA per (batch, q-head, 128-row Q tile); heavy causal tiles are launched first;
+//   * one CTA per (batch, q-head, 128-row Q tile), head-major so a head's K / V stay in L2;
+//     heavy causal tiles of a head are launched first;
 //   * warp 4 loads Q once and streams K / V blocks of 128 keys through a 2-deep TMA ring;
 //   * warp 5 owns TMEM (O: D columns, three S buffers of 128 columns) and issues
 //       S_j = Q K_j^T            (A = Q, B = K, both K-major, from shared memory)
@@ -32,8 +33,9 @@
 namespace ntb {
 namespace fmha {
 
-constexpr int BLK = 128;         // query rows per CTA and keys per KV block
-constexpr int kThreads = 192;    // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr int BLK = 128;         // query rows per Q tile and keys per KV block
+constexpr int kTiles = 2;        // Q tiles per CTA (ping-pong between two softmax warpgroups)
+constexpr int kThreads = 320;    // warps 0-3 softmax tile 0, 4-7 softmax tile 1, 8 TMA, 9 MMA
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;
 
@@ -41,7 +43,7 @@ struct Params {
   int B, Hq, Hkv, Sq, Skv, D;
   int group;        // Hq / Hkv
   int causal;       // 0 none, 1 upper-left, 2 lower-right
-  int nq;           // q tiles per head
+  int nq;           // CTAs per head (each covers kTiles * BLK query rows)
   float scale_log2; // scale * log2(e)
   void* o;
   int64_t o_b, o_h, o_s;  // output strides (unit inner stride)
@@ -53,13 +55,15 @@ struct Smem {
   static constexpr int SUB = BLK * 128;              // one [128 rows][128 B] swizzled sub-tile
   static constexpr int NSUB = D / 64;                // 64-element chunks of head_dim
   static constexpr int TILE = SUB * NSUB;            // Q, K or V tile
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = TILE;
-  static constexpr int V_OFF = 3 * TILE;
-  static constexpr int BAR_OFF = 5 * TILE;
-  static constexpr int TOTAL = 5 * TILE + 1024 + 256;
+  static constexpr int Q_OFF = 0;                    // kTiles Q tiles
+  static constexpr int K_OFF = kTiles * TILE;        // 2 stages
+  static constexpr int V_OFF = K_OFF + 2 * TILE;     // 2 stages
+  static constexpr int BAR_OFF = V_OFF + 2 * TILE;
+  static constexpr int TOTAL = BAR_OFF + 1024 + 256;
 };
 
+// KV blocks a 128-row Q tile starting at q0 must visit (causal tiles skip blocks wholly above
+// the diagonal).
 __device__ __forceinline__ int num_kv_blocks(const Params& p, int q0) {
   int nb = (p.Skv + BLK - 1) / BLK;
   if (p.causal) {
@@ -84,6 +88,10 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// TMEM columns: S_t at 128 t (P_t written over its first 64 columns), O_t at 256 + 128 t.
+constexpr uint32_t kSCol = 0;
+constexpr uint32_t kOCol = 256;
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -91,34 +99,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   using S = Smem<D>;
   constexpr uint32_t kFormat = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t TMEM_COLS = 512;
-  constexpr uint32_t O_COL = 0;
-  constexpr uint32_t S_COL0 = 128;  // S buffer b at S_COL0 + 128 * b, b = 0..2
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + S::Q_OFF;
-  uint8_t* sK = smem + S::K_OFF;  // 2 stages
-  uint8_t* sV = smem + S::V_OFF;  // 2 stages
+  uint8_t* sK = smem + S::K_OFF;
+  uint8_t* sV = smem + S::V_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_full = bars + 1;   // [2] ring stages
   uint64_t* k_empty = bars + 3;  // [2]
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [3]
-  uint64_t* p_full = bars + 12;   // [3]
-  uint64_t* pv_done = bars + 15;  // [3]: PV_j commits to pv_done[j % 3]
-  uint64_t* done_bar = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t* s_full = bars + 9;   // [tile]: S_t(j) in TMEM
+  uint64_t* p_full = bars + 11;  // [tile]: P_t(j) written by the 128 softmax threads of tile t
+  uint64_t* pv_done = bars + 13; // [tile]: O_t += P_t(j) V_j complete (phase j)
+  uint64_t* done_bar = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh_count = p.B * p.Hq;
-  const int qt = p.nq - 1 - (int)(blockIdx.x / bh_count);  // heavy (late) tiles first
-  const int bh = (int)(blockIdx.x % bh_count);
+  // Head-major order (a head's K / V stay in L2 while its Q tiles run), heavy (late) causal
+  // tiles first within each head.
+  const int bh = (int)(blockIdx.x / p.nq);
+  const int qc = p.nq - 1 - (int)(blockIdx.x % p.nq);
   const int b = bh / p.Hq, hq = bh % p.Hq, hkv = hq / p.group;
-  const int q0 = qt * BLK;
-  const int nkv = num_kv_blocks(p, q0);
+  const int q0 = qc * kTiles * BLK;
+  int nkv_t[kTiles];
+#pragma unroll
+  for (int t = 0; t < kTiles; ++t) nkv_t[t] = num_kv_blocks(p, q0 + t * BLK);
+  const int nkv = nkv_t[kTiles - 1];  // the later tile needs at least as many blocks
 
   if (threadIdx.x == 0) {
     sm100::mbar_init(q_full, 1);
@@ -128,16 +138,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::mbar_init(&v_full[i], 1);
       sm100::mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 3; ++i) {
-      sm100::mbar_init(&s_full[i], 1);
-      sm100::mbar_init(&p_full[i], 128);
-      sm100::mbar_init(&pv_done[i], 1);
+    for (int t = 0; t < kTiles; ++t) {
+      sm100::mbar_init(&s_full[t], 1);
+      sm100::mbar_init(&p_full[t], 128);
+      sm100::mbar_init(&pv_done[t], 1);
     }
     sm100::mbar_init(done_bar, 1);
     *abort_flag = 0;
     sm100::fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     sm100::tmem_alloc(tmem_slot, TMEM_COLS);
     sm100::tmem_relinquish();
   }
@@ -146,14 +156,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------------ TMA producer ----
     if (lane == 0 && nkv > 0) {
       uint32_t armed_k = 0, armed_v = 0, par_k = 0, par_v = 0;
       bool ok = true;
-      sm100::mbar_arrive_expect_tx(q_full, S::TILE);
+      sm100::mbar_arrive_expect_tx(q_full, kTiles * S::TILE);
 #pragma unroll
-      for (int c = 0; c < S::NSUB; ++c) sm100::tma_load_4d(sQ + c * S::SUB, &tq, q_full, c * 64, q0, hq, b);
+      for (int t = 0; t < kTiles; ++t)
+#pragma unroll
+        for (int c = 0; c < S::NSUB; ++c)
+          sm100::tma_load_4d(sQ + t * S::TILE + c * S::SUB, &tq, q_full, c * 64, q0 + t * BLK, hq, b);
       for (int j = 0; j < nkv && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -173,72 +186,75 @@ __global__ void __launch_bounds__(kThreads, 1)
           sm100::tma_load_4d(sV + st * S::TILE + c * S::SUB, &tv, &v_full[st], c * 64, j * BLK, hkv, b);
       }
       sm100::mbar_wait_unwind(q_full, 0);
-      for (int s = 0; s < 2; ++s) {
-        if (armed_k & (1u << s)) sm100::mbar_wait_unwind(&k_full[s], (par_k >> s) & 1u);
-        if (armed_v & (1u << s)) sm100::mbar_wait_unwind(&v_full[s], (par_v >> s) & 1u);
+      for (int st = 0; st < 2; ++st) {
+        if (armed_k & (1u << st)) sm100::mbar_wait_unwind(&k_full[st], (par_k >> st) & 1u);
+        if (armed_v & (1u << st)) sm100::mbar_wait_unwind(&v_full[st], (par_v >> st) & 1u);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------------- MMA issuer ----
+    // Order: S_0(0), S_1(0), then per block j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1).  While one
+    // softmax warpgroup works on its tile the tensor core runs the other tile's PV and next S.
+    // tcgen05.mma operations of one thread execute in issue order, so S_t(j+1) is issued right
+    // after PV_t(j) even though it overwrites the TMEM columns PV_t(j) reads P_t(j) from.
     constexpr uint32_t idesc_qk = sm100::instr_desc(kFormat, false, false, BLK, BLK);
     constexpr uint32_t idesc_pv = sm100::instr_desc(kFormat, false, true, BLK, D);
     bool ok = nkv > 0 && sm100::mbar_wait(q_full, 0, abort_flag, p.err);
     sm100::tc_fence_after();
     const uint32_t q_addr = sm100::smem_u32(sQ);
-    int issued_s = 0;  // S blocks issued
-    auto issue_s = [&](int j) -> bool {
+    // S_t(j) = Q_t K_j^T; the last tile to use K_j releases its stage.
+    auto issue_s = [&](int t, int j, bool release_k) -> bool {
       const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (j >= 3) {  // S buffer j%3 held P_{j-3}: wait for PV_{j-3} to finish reading it
-        if (!sm100::mbar_wait(&pv_done[j % 3], (uint32_t)(((j - 3) / 3) & 1), abort_flag, p.err)) return false;
+      if (t == 0 || nkv_t[0] <= j) {  // first user of K_j waits for it
+        if (!sm100::mbar_wait(&k_full[st], (uint32_t)((j >> 1) & 1), abort_flag, p.err)) return false;
+        sm100::tc_fence_after();
       }
-      if (!sm100::mbar_wait(&k_full[st], ph, abort_flag, p.err)) return false;
-      sm100::tc_fence_after();
       if (lane == 0) {
         const uint32_t k_addr = sm100::smem_u32(sK + st * S::TILE);
-        const uint32_t d_tmem = tmem + S_COL0 + 128u * (uint32_t)(j % 3);
+        const uint32_t qt_addr = q_addr + t * S::TILE;
+        const uint32_t d_tmem = tmem + kSCol + 128u * t;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * S::SUB + (kk & 3) * 32;
-          sm100::mma_f16(d_tmem, sm100::smem_desc(q_addr + off, 16, 1024),
+          sm100::mma_f16(d_tmem, sm100::smem_desc(qt_addr + off, 16, 1024),
                          sm100::smem_desc(k_addr + off, 16, 1024), idesc_qk, kk != 0);
         }
-        sm100::mma_commit(&k_empty[st]);
-        sm100::mma_commit(&s_full[j % 3]);
+        sm100::mma_commit(&s_full[t]);
+        if (release_k) sm100::mma_commit(&k_empty[st]);
       }
       __syncwarp();
       return true;
     };
-    auto issue_pv = [&](int j) -> bool {
+    // O_t += P_t(j) V_j; the last tile to use V_j releases its stage.
+    auto issue_pv = [&](int t, int j, bool first_v, bool release_v) -> bool {
       const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!sm100::mbar_wait(&p_full[j % 3], (uint32_t)((j / 3) & 1), abort_flag, p.err)) return false;
-      if (!sm100::mbar_wait(&v_full[st], ph, abort_flag, p.err)) return false;
+      if (!sm100::mbar_wait(&p_full[t], (uint32_t)(j & 1), abort_flag, p.err)) return false;
+      if (first_v && !sm100::mbar_wait(&v_full[st], (uint32_t)((j >> 1) & 1), abort_flag, p.err)) return false;
       sm100::tc_fence_after();
       if (lane == 0) {
         const uint32_t v_addr = sm100::smem_u32(sV + st * S::TILE);
-        const uint32_t p_tmem = tmem + S_COL0 + 128u * (uint32_t)(j % 3);
+        const uint32_t p_tmem = tmem + kSCol + 128u * t;
+        const uint32_t o_tmem = tmem + kOCol + 128u * t;
 #pragma unroll
-        for (int kk = 0; kk < BLK / 16; ++kk) {
-          sm100::mma_f16_ts(tmem + O_COL, p_tmem + kk * 8,
-                            sm100::smem_desc(v_addr + kk * 16 * 128, S::SUB, 1024), idesc_pv,
-                            (j | kk) != 0);
-        }
-        sm100::mma_commit(&v_empty[st]);
-        sm100::mma_commit(&pv_done[j % 3]);
+        for (int kk = 0; kk < BLK / 16; ++kk)
+          sm100::mma_f16_ts(o_tmem, p_tmem + kk * 8, sm100::smem_desc(v_addr + kk * 16 * 128, S::SUB, 1024),
+                            idesc_pv, (j | kk) != 0);
+        sm100::mma_commit(&pv_done[t]);
+        if (release_v) sm100::mma_commit(&v_empty[st]);
       }
       __syncwarp();
       return true;
     };
-    if (ok) ok = issue_s(0);
-    if (ok && nkv > 1) ok = issue_s(1);
-    issued_s = nkv > 1 ? 2 : 1;
+    if (ok && nkv_t[0] > 0) ok = issue_s(0, 0, false);
+    if (ok) ok = issue_s(1, 0, true);
     for (int j = 0; ok && j < nkv; ++j) {
-      ok = issue_pv(j);
-      if (ok && issued_s < nkv) {
-        ok = issue_s(issued_s);
-        ++issued_s;
+      const bool t0 = j < nkv_t[0];
+      if (t0) {
+        ok = issue_pv(0, j, true, false);
+        if (ok && j + 1 < nkv_t[0]) ok = issue_s(0, j + 1, false);
       }
+      if (ok) ok = issue_pv(1, j, !t0, true);
+      if (ok && j + 1 < nkv) ok = issue_s(1, j + 1, true);
     }
     if (lane == 0) {
       sm100::mma_commit(done_bar);
@@ -246,90 +262,94 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // --------------------------------------------------------------- softmax warps ----
-    const int row = q0 + warp * 32 + lane;  // warp w reads TMEM lanes 32w..32w+31
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    // ------------------------------------------------------- softmax warpgroups ----
+    const int t = warp >> 2;                       // Q tile of this warpgroup
+    const int wq = warp & 3;                       // TMEM lane quarter
+    const int row = q0 + t * BLK + wq * 32 + lane; // query row of this thread
+    const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
+    const uint32_t s_tmem = tmem + kSCol + 128u * t + lane_addr;
+    const uint32_t o_tmem = tmem + kOCol + 128u * t + lane_addr;
     const int off = p.causal == 2 ? p.Skv - p.Sq : 0;
+    const int nkv_mine = nkv_t[t];
+    const int kmax = p.causal ? min(p.Skv - 1, row + off) : p.Skv - 1;
     float m_used = -INFINITY;  // reference max of P and O (base-2 units)
     float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      if (!sm100::mbar_wait(&s_full[j % 3], (uint32_t)((j / 3) & 1), abort_flag, p.err)) { ok = false; break; }
+    for (int j = 0; j < nkv_mine; ++j) {
+      if (!sm100::mbar_wait(&s_full[t], (uint32_t)(j & 1), abort_flag, p.err)) { ok = false; break; }
       sm100::tc_fence_after();
-      const uint32_t s_tmem = tmem + S_COL0 + 128u * (uint32_t)(j % 3) + lane_addr;
-      float s[128];
+      const int k0 = j * BLK;
+      const bool need_mask = (k0 + BLK - 1 > kmax);
+      // pass 1: row max (8 independent chains)
+      float mx8[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mx8[c] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
         sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, r);
         sm100::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 32; ++i) {
+          float v = __uint_as_float(r[i]);
+          if (need_mask && k0 + c * 32 + i > kmax) v = -INFINITY;
+          mx8[i & 7] = fmaxf(mx8[i & 7], v);
+        }
       }
-      const int k0 = j * BLK;
-      const bool need_mask = (k0 + BLK > p.Skv) || (p.causal && k0 + BLK - 1 > q0 + off);
-      if (need_mask) {
-        const int kmax = p.causal ? min(p.Skv - 1, row + off) : p.Skv - 1;
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (k0 + i > kmax) s[i] = -INFINITY;
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_blk = mx * p.scale_log2;
       // Rescale O and l only when the max grows by more than the threshold.
       const bool grow = m_blk > m_used + kRescaleThreshold;
       if (__any_sync(0xffffffffu, grow && j > 0)) {
-        float alpha = 1.f;
-        if (grow) alpha = exp2f(m_used - m_blk);
-        // PV_{j-1} (and, by commit order, every earlier PV) must have finished writing O.
-        if (!sm100::mbar_wait(&pv_done[(j - 1) % 3], (uint32_t)(((j - 1) / 3) & 1), abort_flag, p.err)) {
-          ok = false;
-          break;
-        }
+        const float alpha = grow ? exp2f(m_used - m_blk) : 1.f;
+        // PV_t(j-1) (and, by commit order, every earlier PV of this tile) must be complete.
+        if (!sm100::mbar_wait(&pv_done[t], (uint32_t)((j - 1) & 1), abort_flag, p.err)) { ok = false; break; }
         sm100::tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
-          sm100::tmem_ld_32x32b_x32(tmem + O_COL + c * 32 + lane_addr, r);
+          sm100::tmem_ld_32x32b_x32(o_tmem + c * 32, r);
           sm100::tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          sm100::tmem_st_32x32b_x32(tmem + O_COL + c * 32 + lane_addr, r);
+          sm100::tmem_st_32x32b_x32(o_tmem + c * 32, r);
         }
         sm100::tmem_st_wait();
         l *= alpha;
       }
       if (grow) m_used = m_blk;
       const float m_ref = m_used == -INFINITY ? 0.f : m_used;
-      float sum = 0.f;
-      uint32_t pk[64];
+      // pass 2: P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float p0 = exp2f(fmaf(s[2 * i], p.scale_log2, -m_ref));
-        const float p1 = exp2f(fmaf(s[2 * i + 1], p.scale_log2, -m_ref));
-        sum += p0 + p1;
-        pk[i] = pack2<T>(p0, p1);
-      }
-      l += sum;
-      const uint32_t p_tmem = tmem + S_COL0 + 128u * (uint32_t)(j % 3) + lane_addr;
-      {
+      for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
+        sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, r);
+        sm100::tmem_ld_wait();
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = pk[i];
-        sm100::tmem_st_32x32b_x32(p_tmem, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = pk[32 + i];
-        sm100::tmem_st_32x32b_x32(p_tmem + 32, r);
+        for (int i = 0; i < 16; ++i) {
+          float s0 = __uint_as_float(r[2 * i]), s1 = __uint_as_float(r[2 * i + 1]);
+          if (need_mask) {
+            if (k0 + c * 32 + 2 * i > kmax) s0 = -INFINITY;
+            if (k0 + c * 32 + 2 * i + 1 > kmax) s1 = -INFINITY;
+          }
+          const float p0 = sm100::ex2_approx(fmaf(s0, p.scale_log2, -m_ref));
+          const float p1 = sm100::ex2_approx(fmaf(s1, p.scale_log2, -m_ref));
+          sum4[i & 3] += p0 + p1;
+          pk[i] = pack2<T>(p0, p1);
+        }
+        sm100::tmem_st_32x32b_x16(s_tmem + c * 16, pk);
       }
+      l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       sm100::tmem_st_wait();
       sm100::tc_fence_before();
-      sm100::mbar_arrive(&p_full[j % 3]);
+      sm100::mbar_arrive(&p_full[t]);
     }
     // Epilogue: O / l, written as this row's D contiguous elements.
-    if (ok && nkv > 0)
-      ok = sm100::mbar_wait(&pv_done[(nkv - 1) % 3], (uint32_t)(((nkv - 1) / 3) & 1), abort_flag, p.err);
+    if (ok && nkv_mine > 0)
+      ok = sm100::mbar_wait(&pv_done[t], (uint32_t)((nkv_mine - 1) & 1), abort_flag, p.err);
     sm100::tc_fence_after();
     if (ok) {
       const float inv = 1.f / l;  // l == 0 (fully masked row) gives NaN, as torch does
@@ -337,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
-        if (nkv > 0) {
-          sm100::tmem_ld_32x32b_x32(tmem + O_COL + c * 32 + lane_addr, r);
+        if (nkv_mine > 0) {
+          sm100::tmem_ld_32x32b_x32(o_tmem + c * 32, r);
           sm100::tmem_ld_wait();
         } else {
 #pragma unroll
@@ -358,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -580,7 +600,7 @@ extern "C" int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor*
   p.Skv = (int)k->shape[2];
   p.group = p.Hq / p.Hkv;
   p.causal = causal_variant;
-  p.nq = (p.Sq + BLK - 1) / BLK;
+  p.nq = (p.Sq + kTiles * BLK - 1) / (kTiles * BLK);
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.o = o->data;
   p.o_b = o->stride[0];

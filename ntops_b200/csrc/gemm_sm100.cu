@@ -7,8 +7,9 @@
 //
 // sm_100a design (bf16 / fp16, and fp32 as TF32):
 //   * persistent kernel, one 192-thread CTA per SM, static tile schedule (tile = blockIdx.x +
-//     i * gridDim.x) rasterised in bands of 8 M-blocks so concurrently running tiles share A
-//     rows and B columns in L2;
+//     i * gridDim.x) rasterised in bands of 8-64 M-blocks (as many as keep the band's A rows
+//     within ~48 MB of L2) so concurrently running tiles share A rows and B columns in L2 and B
+//     streams from DRAM once per band;
 //   * warp 0 issues TMA loads (128-byte swizzle, zero fill past the edges) into a STAGES-deep
 //     ring of shared-memory stages guarded by full/empty mbarriers;
 //   * warp 1 allocates 2 x BN TMEM columns (a double-buffered 128 x BN fp32 accumulator) and one
@@ -34,15 +35,22 @@ constexpr int BM = 128;
 constexpr int kRowBytes = 128;  // one swizzle atom row: BK elements of the operand type
 constexpr int kThreads = 192;
 
+// Epilogues: plain (alpha * acc + beta * C), or SwiGLU — the B operand holds gate and up
+// weight columns interleaved in blocks of BN/2, and each tile writes silu(gate) * up.
+constexpr int kEpiPlain = 0;
+constexpr int kEpiSwiGLU = 1;
+
 struct Params {
   int M, N, K, batch;
   int mblocks, nblocks, kblocks, tiles;
   int a_mn, b_mn;  // operand is MN-major (else K-major)
+  int band;        // M-blocks per raster band (power of two)
   void* d;
   int64_t d_bs, d_ms;  // output: batch and row strides (unit column stride)
   const void* c;       // optional addend (same dtype as d), any strides (0 = broadcast)
   int64_t c_bs, c_ms, c_ns;
   float alpha, beta;
+  int n_out;  // SwiGLU epilogue: output columns (= N / 2)
   unsigned int* err;
 };
 
@@ -60,7 +68,7 @@ __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& b, i
   const int per_batch = p.mblocks * p.nblocks;
   b = tile / per_batch;
   int t = tile - b * per_batch;
-  constexpr int G = 8;  // M-blocks per raster band
+  const int G = p.band;  // M-blocks per raster band
   const int band = t / (G * p.nblocks);
   const int m0 = band * G;
   const int gm = min(G, p.mblocks - m0);
@@ -100,8 +108,39 @@ __device__ __forceinline__ void store_row_chunk(const Params& p, TD* drow, const
   }
 }
 
+__device__ __forceinline__ float silu_f(float g) {
+  // silu(g) = g / (1 + e^-g), hardware exp2 / reciprocal (the result is rounded to 16 bits)
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-g * 1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + e));
+  return g * r;
+}
+
+// SwiGLU epilogue of one 32-column chunk: out = silu(gate) * up.
+template <typename TD>
+__device__ __forceinline__ void store_swiglu_chunk(const Params& p, TD* drow, int col0, const uint32_t (&g)[32],
+                                                   const uint32_t (&u)[32]) {
+  float o[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) o[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+  constexpr int V = 16 / sizeof(TD);
+  if (col0 + 32 <= p.n_out && (reinterpret_cast<uintptr_t>(drow + col0) % 16) == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; j += V) {
+      ew::Vec<TD, V> vv;
+#pragma unroll
+      for (int e = 0; e < V; ++e) vv.v[e] = cvt<TD>(o[j + e]);
+      *reinterpret_cast<ew::Vec<TD, V>*>(drow + col0 + j) = vv;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < p.n_out) drow[col0 + j] = cvt<TD>(o[j]);
+  }
+}
+
 // T: operand element type (__half / __nv_bfloat16 / float for TF32); TD: output type.
-template <typename T, typename TD, int BN, int STAGES>
+template <typename T, typename TD, int BN, int STAGES, int EPI = kEpiPlain>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    Params p) {
@@ -269,17 +308,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TD* crow = nullptr;
       if (p.c != nullptr && p.beta != 0.f)
         crow = reinterpret_cast<const TD*>(p.c) + (int64_t)b * p.c_bs + (int64_t)row * p.c_ms;
+      if (EPI == kEpiSwiGLU) {
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t r[32];
-        sm100::tmem_ld_32x32b_x32(tmem_base + acc * BN + ch * 32 + ((uint32_t)(q * 32) << 16), r);
-        sm100::tmem_ld_wait();
-        const int col0 = nb * BN + ch * 32;
-        if (row < p.M && col0 < p.N) {
-          float v[32];
+        for (int ch = 0; ch < BN / 64; ++ch) {
+          uint32_t g[32], u[32];
+          const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+          sm100::tmem_ld_32x32b_x32(tmem_base + acc * BN + ch * 32 + lane_off, g);
+          sm100::tmem_ld_32x32b_x32(tmem_base + acc * BN + BN / 2 + ch * 32 + lane_off, u);
+          sm100::tmem_ld_wait();
+          const int col0 = nb * (BN / 2) + ch * 32;
+          if (row < p.M && col0 < p.n_out) store_swiglu_chunk<TD>(p, drow, col0, g, u);
+        }
+      } else {
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t r[32];
+          sm100::tmem_ld_32x32b_x32(tmem_base + acc * BN + ch * 32 + ((uint32_t)(q * 32) << 16), r);
+          sm100::tmem_ld_wait();
+          const int col0 = nb * BN + ch * 32;
+          if (row < p.M && col0 < p.N) {
+            float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          store_row_chunk<TD>(p, drow, crow, col0, v);
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            store_row_chunk<TD>(p, drow, crow, col0, v);
+          }
         }
       }
       sm100::tc_fence_before();
@@ -361,7 +413,7 @@ struct Operand {
   int64_t bs, s_outer, s_k;  // batch stride, stride along M (A) / N (B), stride along K
 };
 
-template <typename T, typename TD, int BN, int STAGES>
+template <typename T, typename TD, int BN, int STAGES, int EPI = kEpiPlain>
 int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& oa, const Operand& ob,
               CUtensorMapDataType tdt, cudaStream_t st) {
   using S = Smem<BN, STAGES, sizeof(T)>;
@@ -387,7 +439,15 @@ int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& 
   p.mblocks = (p.M + BM - 1) / BM;
   p.nblocks = (p.N + BN - 1) / BN;
   p.tiles = p.mblocks * p.nblocks * p.batch;
-  auto kernel = gemm_tc_kernel<T, TD, BN, STAGES>;
+  // Raster band: as many M-blocks as keep the band's A rows (BM x K) within ~48 MB of L2, so A
+  // is read from DRAM once and B once per band (8..64 M-blocks).
+  {
+    const int64_t a_band_bytes = (int64_t)BM * p.K * es;
+    int g = 64;
+    while (g > 8 && (int64_t)g * a_band_bytes > (48ll << 20)) g >>= 1;
+    p.band = g;
+  }
+  auto kernel = gemm_tc_kernel<T, TD, BN, STAGES, EPI>;
   static std::atomic<uint64_t> attr_set{0};  // bit per device; setting twice is harmless
   const int dev = current_device();
   const uint64_t bit = 1ull << (dev & 63);
@@ -548,4 +608,52 @@ extern "C" int ntb_gemm(const NtbTensor* a, const NtbTensor* bm, const NtbTensor
   }
   NTB_DISPATCH_FLOAT(a->dtype, return launch_simt<scalar_t>(a, bm, p, oa, ob, st));
   return NTB_OK;
+}
+
+extern "C" int ntb_gemm_swiglu(const NtbTensor* a, const NtbTensor* w, const NtbTensor* d, void* stream) {
+  using namespace ntb;
+  using namespace ntb::gemm;
+  int rc;
+  if ((rc = check_tensor(a, "input")) != NTB_OK) return rc;
+  if ((rc = check_tensor(w, "packed weight")) != NTB_OK) return rc;
+  if ((rc = check_tensor(d, "out")) != NTB_OK) return rc;
+  NTB_ARG(a->ndim == 2 && w->ndim == 2 && d->ndim == 2, "swiglu gemm takes 2-D tensors");
+  NTB_ARG(a->shape[1] == w->shape[0], "inner dimensions differ");
+  NTB_ARG(w->shape[1] % 256 == 0, "packed weight width must be a multiple of 256 (gate/up blocks of 128)");
+  NTB_ARG(d->shape[0] == a->shape[0] && d->shape[1] * 2 == w->shape[1], "output must be [M, N/2]");
+  NTB_ARG(d->stride[1] == 1 || d->shape[1] == 1, "output must have a unit column stride");
+  NTB_UNSUP(a->dtype == w->dtype && d->dtype == a->dtype && (a->dtype == NTB_BF16 || a->dtype == NTB_F16),
+            "swiglu gemm needs bf16 or fp16 operands and output of the same dtype");
+  Params p = {};
+  p.batch = 1;
+  p.M = (int)a->shape[0];
+  p.K = (int)a->shape[1];
+  p.N = (int)w->shape[1];
+  p.n_out = p.N / 2;
+  p.d = d->data;
+  p.d_bs = 0;
+  p.d_ms = d->stride[0];
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  p.err = device_error_ptr();
+  if ((int64_t)p.M * p.N == 0) return NTB_OK;
+  NTB_UNSUP(p.K > 0, "K = 0 is not supported by the fused kernel");
+  Operand oa{0, a->stride[0], a->stride[1]};
+  Operand ob{0, w->stride[1], w->stride[0]};
+  const bool a_k = oa.s_k == 1 || p.K == 1, a_mn = oa.s_outer == 1 || p.M == 1;
+  const bool b_k = ob.s_k == 1 || p.K == 1, b_mn = ob.s_outer == 1;
+  NTB_UNSUP((a_k || a_mn) && (b_k || b_mn), "operands need a unit stride along K or M / N");
+  p.a_mn = a_k ? 0 : 1;
+  p.b_mn = b_k ? 0 : 1;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a->dtype == NTB_BF16) {
+    NTB_UNSUP(tma_operand_ok<__nv_bfloat16>(a, oa, p.a_mn, p.M, p.K, 1) &&
+                  tma_operand_ok<__nv_bfloat16>(w, ob, p.b_mn, p.N, p.K, 1),
+              "operand rows are not 16-byte aligned for TMA");
+    return launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4, kEpiSwiGLU>(a, w, p, oa, ob,
+                                                                        CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
+  }
+  NTB_UNSUP(tma_operand_ok<__half>(a, oa, p.a_mn, p.M, p.K, 1) && tma_operand_ok<__half>(w, ob, p.b_mn, p.N, p.K, 1),
+            "operand rows are not 16-byte aligned for TMA");
+  return launch_tc<__half, __half, 256, 4, kEpiSwiGLU>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
 }

@@ -3,9 +3,9 @@
 // Reference algorithm (ntops): kernels/rms_norm.py:10-20 — fp32 sum of squares over the row,
 // rms = sqrt(sum / n + eps), y = x / rms * w; kernels/layer_norm.py:11-31 — fp32 mean, biased
 // variance of (x - mean), y = (x - mean) / sqrt(var + eps) * w + b.  Both read each row once
-// from HBM here (register-resident row, see rowreduce.cuh); the reference reads it 2 and 3
-// times.  Statistics are fp32 for half/bf16/fp32 inputs and fp64 for fp64 inputs.
-#include "rowreduce.cuh"
+// from HBM here (a bulk copy stages it in shared memory, see rowstage.cuh) and reduces once;
+// the reference reads it 2 and 3 times.  Statistics are fp32 for half/bf16/fp32 inputs and fp64 for fp64.
+#include "rowstage.cuh"
 
 namespace ntb {
 namespace {
@@ -14,60 +14,64 @@ template <typename T> struct Acc { using type = float; };
 template <> struct Acc<double> { using type = double; };
 
 // ------------------------------------------------------------------ RMSNorm ---------------
-template <typename T, int VEC, int NCH>
-__global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w,
-                                                        T* __restrict__ y, rr::RowGeom g, double eps) {
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) rms_norm_staged(const T* __restrict__ x, const T* __restrict__ w,
+                                                        T* __restrict__ y, rs::StageGeom g, double eps,
+                                                        unsigned int* err) {
+  extern __shared__ __align__(128) uint8_t dyn[];
   using C = typename Acc<T>::type;
-  __shared__ C red[32];
-  __shared__ C slots[2];
-  const int cs = g.cs;
-  const int rank = (int)(blockIdx.x % cs);
-  const int64_t row = blockIdx.x / cs;
-  const int64_t vecs = g.cols / VEC;
-  const int64_t base = (int64_t)rank * blockDim.x * NCH;
-  C xr[NCH][VEC];
-  bool valid[NCH];
-  rr::load_row<T, C, VEC, NCH>(x + row * g.x_rs, vecs, base, xr, valid);
-  C ss = 0;
+  using R = rr::Sum<C>;
+  using V = ew::Vec<T, VEC>;
+  __shared__ R red[32];
+  __shared__ R slot;
+  bool pending = false;
+  rs::staged_rows<T>(x, g, dyn, err, [&](int64_t row, const T* sx, int64_t n, int64_t base) {
+    const int64_t nv = n / VEC;
+    C ss[2] = {C(0), C(0)};
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
+      const V xv = reinterpret_cast<const V*>(sx)[v];
 #pragma unroll
-  for (int k = 0; k < NCH; ++k)
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) ss += xr[k][e] * xr[k][e];
-  ss = rr::row_allreduce(ss, rr::SumOp{}, red, slots, 0, cs);
-  const C rinv = C(1) / rr::c_sqrt<C>(ss / C(g.cols) + C(eps));
-  T* yrow = y + row * g.y_rs;
-#pragma unroll
-  for (int k = 0; k < NCH; ++k) {
-    if (!valid[k]) continue;
-    int64_t v = base + (int64_t)k * blockDim.x + threadIdx.x;
-    ew::Vec<T, VEC> out;
-    if (w != nullptr) {
-      ew::Vec<T, VEC> wv = reinterpret_cast<const ew::Vec<T, VEC>*>(w)[v];
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(xr[k][e] * rinv * cvt<C>(wv.v[e]));
-    } else {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(xr[k][e] * rinv);
+      for (int e = 0; e < VEC; ++e) {
+        const C c = cvt<C>(xv.v[e]);
+        ss[e & 1] += c * c;
+      }
     }
-    ew::store_cs(reinterpret_cast<ew::Vec<T, VEC>*>(yrow) + v, out);
-  }
-  rr::cluster_exit_barrier(cs);
+    const C tot = rr::row_allreduce(R{ss[0] + ss[1]}, red, &slot, g.cs, pending).v;
+    const C rinv = C(1) / rr::c_sqrt<C>(tot / C(g.cols) + C(eps));
+    V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + base);
+    const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + base) : nullptr;
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
+      const V xv = reinterpret_cast<const V*>(sx)[v];
+      V out;
+      if (wrow != nullptr) {
+        const V wv = wrow[v];
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(cvt<C>(xv.v[e]) * rinv * cvt<C>(wv.v[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(cvt<C>(xv.v[e]) * rinv);
+      }
+      ew::store_cs(yrow + v, out);
+    }
+  });
+  rr::cluster_exit(g.cs, pending);
 }
 
-// Rows too long for the register-resident kernel: three strided passes, later ones from L2.
+// Rows too long for the register-resident kernel: strided passes, later ones from L2.
 template <typename T>
 __global__ void __launch_bounds__(1024) rms_norm_looped(const T* __restrict__ x, const T* __restrict__ w,
                                                         T* __restrict__ y, rr::RowGeom g, double eps) {
   using C = typename Acc<T>::type;
-  __shared__ C red[32];
+  using R = rr::Sum<C>;
+  __shared__ R red[32];
   for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x) {
     const T* xrow = x + row * g.x_rs;
     C ss = 0;
     for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x) {
-      C v = cvt<C>(xrow[i]);
+      const C v = cvt<C>(xrow[i]);
       ss += v * v;
     }
-    ss = rr::block_allreduce(ss, rr::SumOp{}, red);
+    ss = rr::block_allreduce(R{ss}, red).v;
     const C rinv = C(1) / rr::c_sqrt<C>(ss / C(g.cols) + C(eps));
     T* yrow = y + row * g.y_rs;
     for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x) {
@@ -79,58 +83,62 @@ __global__ void __launch_bounds__(1024) rms_norm_looped(const T* __restrict__ x,
 }
 
 // ---------------------------------------------------------------- LayerNorm ---------------
-template <typename T, int VEC, int NCH>
-__global__ void __launch_bounds__(256) layer_norm_kernel(const T* __restrict__ x, const T* __restrict__ w,
+// One reduction: every thread forms the exact (count, mean, M2) of its own elements in two
+// passes over the staged row, and the triples merge across threads, warps and CTAs with Chan's
+// formula.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) layer_norm_staged(const T* __restrict__ x, const T* __restrict__ w,
                                                           const T* __restrict__ b, T* __restrict__ y,
-                                                          rr::RowGeom g, double eps) {
+                                                          rs::StageGeom g, double eps, unsigned int* err) {
+  extern __shared__ __align__(128) uint8_t dyn[];
   using C = typename Acc<T>::type;
-  __shared__ C red[32];
-  __shared__ C slots[2];
-  const int cs = g.cs;
-  const int rank = (int)(blockIdx.x % cs);
-  const int64_t row = blockIdx.x / cs;
-  const int64_t vecs = g.cols / VEC;
-  const int64_t base = (int64_t)rank * blockDim.x * NCH;
-  C xr[NCH][VEC];
-  bool valid[NCH];
-  rr::load_row<T, C, VEC, NCH>(x + row * g.x_rs, vecs, base, xr, valid);
-  C s = 0;
+  using R = rr::Welford<C>;
+  using V = ew::Vec<T, VEC>;
+  __shared__ R red[32];
+  __shared__ R slot;
+  bool pending = false;
+  rs::staged_rows<T>(x, g, dyn, err, [&](int64_t row, const T* sx, int64_t n, int64_t base) {
+    const int64_t nv = n / VEC;
+    C s[2] = {C(0), C(0)};
+    int cnt = 0;
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
+      const V xv = reinterpret_cast<const V*>(sx)[v];
+      cnt += VEC;
 #pragma unroll
-  for (int k = 0; k < NCH; ++k)
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) s += xr[k][e];
-  s = rr::row_allreduce(s, rr::SumOp{}, red, slots, 0, cs);
-  const C mean = s / C(g.cols);
-  C sq = 0;
-#pragma unroll
-  for (int k = 0; k < NCH; ++k) {
-    if (!valid[k]) continue;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      C d = xr[k][e] - mean;
-      sq += d * d;
+      for (int e = 0; e < VEC; ++e) s[e & 1] += cvt<C>(xv.v[e]);
     }
-  }
-  sq = rr::row_allreduce(sq, rr::SumOp{}, red, slots, 1, cs);
-  const C rstd = C(1) / rr::c_sqrt<C>(sq / C(g.cols) + C(eps));
-  T* yrow = y + row * g.y_rs;
+    const C mean_t = cnt ? (s[0] + s[1]) / C(cnt) : C(0);
+    C m2[2] = {C(0), C(0)};
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
+      const V xv = reinterpret_cast<const V*>(sx)[v];
 #pragma unroll
-  for (int k = 0; k < NCH; ++k) {
-    if (!valid[k]) continue;
-    int64_t v = base + (int64_t)k * blockDim.x + threadIdx.x;
-    ew::Vec<T, VEC> wv, bv, out;
-    if (w != nullptr) wv = reinterpret_cast<const ew::Vec<T, VEC>*>(w)[v];
-    if (b != nullptr) bv = reinterpret_cast<const ew::Vec<T, VEC>*>(b)[v];
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      C r = (xr[k][e] - mean) * rstd;
-      if (w != nullptr) r *= cvt<C>(wv.v[e]);
-      if (b != nullptr) r += cvt<C>(bv.v[e]);
-      out.v[e] = cvt<T>(r);
+      for (int e = 0; e < VEC; ++e) {
+        const C d = cvt<C>(xv.v[e]) - mean_t;
+        m2[e & 1] += d * d;
+      }
     }
-    ew::store_cs(reinterpret_cast<ew::Vec<T, VEC>*>(yrow) + v, out);
-  }
-  rr::cluster_exit_barrier(cs);
+    const R st = rr::row_allreduce(R{C(cnt), mean_t, m2[0] + m2[1]}, red, &slot, g.cs, pending);
+    const C mean = st.mean;
+    const C rstd = C(1) / rr::c_sqrt<C>(st.m2 / C(g.cols) + C(eps));
+    V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + base);
+    const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + base) : nullptr;
+    const V* brow = b != nullptr ? reinterpret_cast<const V*>(b + base) : nullptr;
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
+      const V xv = reinterpret_cast<const V*>(sx)[v];
+      V wv, bv, out;
+      if (wrow != nullptr) wv = wrow[v];
+      if (brow != nullptr) bv = brow[v];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        C r = (cvt<C>(xv.v[e]) - mean) * rstd;  // subtract first: no cancellation
+        if (wrow != nullptr) r *= cvt<C>(wv.v[e]);
+        if (brow != nullptr) r += cvt<C>(bv.v[e]);
+        out.v[e] = cvt<T>(r);
+      }
+      ew::store_cs(yrow + v, out);
+    }
+  });
+  rr::cluster_exit(g.cs, pending);
 }
 
 template <typename T>
@@ -138,18 +146,19 @@ __global__ void __launch_bounds__(1024) layer_norm_looped(const T* __restrict__ 
                                                           const T* __restrict__ b, T* __restrict__ y,
                                                           rr::RowGeom g, double eps) {
   using C = typename Acc<T>::type;
-  __shared__ C red[32];
+  using R = rr::Sum<C>;
+  __shared__ R red[32];
   for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x) {
     const T* xrow = x + row * g.x_rs;
     C s = 0;
     for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x) s += cvt<C>(xrow[i]);
-    const C mean = rr::block_allreduce(s, rr::SumOp{}, red) / C(g.cols);
+    const C mean = rr::block_allreduce(R{s}, red).v / C(g.cols);
     C sq = 0;
     for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x) {
-      C d = cvt<C>(xrow[i]) - mean;
+      const C d = cvt<C>(xrow[i]) - mean;
       sq += d * d;
     }
-    const C rstd = C(1) / rr::c_sqrt<C>(rr::block_allreduce(sq, rr::SumOp{}, red) / C(g.cols) + C(eps));
+    const C rstd = C(1) / rr::c_sqrt<C>(rr::block_allreduce(R{sq}, red).v / C(g.cols) + C(eps));
     T* yrow = y + row * g.y_rs;
     for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x) {
       C r = (cvt<C>(xrow[i]) - mean) * rstd;
@@ -199,12 +208,13 @@ bool vec_ok(const NtbTensor* x, const NtbTensor* y, const NtbTensor* w, const Nt
 template <typename T, int VEC>
 int launch_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTensor* b,
                 const NtbTensor* y, rr::RowGeom g, double eps, cudaStream_t st) {
-  int bt, nch, cs;
   const T* xp = (const T*)x->data;
   const T* wp = w ? (const T*)w->data : nullptr;
   const T* bp = b ? (const T*)b->data : nullptr;
   T* yp = (T*)y->data;
-  if (!rr::plan_row(g.cols / VEC, &bt, &nch, &cs)) {
+  int chunk = 0, cs = 1;
+  if (VEC == 1 || !rs::plan_stage(g.cols, (int)sizeof(T), VEC, &chunk, &cs) ||
+      !rs::stage_aligned(xp, g.x_rs, g.rows, (int)sizeof(T))) {
     int grid = (int)(g.rows < (int64_t)sm_count() * 8 ? g.rows : (int64_t)sm_count() * 8);
     if (layer)
       layer_norm_looped<T><<<grid, 512, 0, st>>>(xp, wp, bp, yp, g, eps);
@@ -213,21 +223,15 @@ int launch_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTen
     NTB_LAUNCH_CHECK();
     return NTB_OK;
   }
-  g.cs = cs;
-#define NTB_NORM_CASE(N)                                                                          \
-  case N:                                                                                         \
-    if (layer)                                                                                    \
-      return rr::launch_rows(layer_norm_kernel<T, VEC, N>, g.rows, bt, cs, st, xp, wp, bp, yp, g, eps); \
-    return rr::launch_rows(rms_norm_kernel<T, VEC, N>, g.rows, bt, cs, st, xp, wp, yp, g, eps);
-  switch (nch) {
-    NTB_NORM_CASE(1)
-    NTB_NORM_CASE(2)
-    NTB_NORM_CASE(4)
-    NTB_NORM_CASE(8)
-  }
-#undef NTB_NORM_CASE
-  set_error("internal: bad row plan");
-  return NTB_ERR_INVALID;
+  rs::StageGeom sg{g.rows, g.cols, g.x_rs, g.y_rs, cs, chunk};
+  const int nvec = chunk / VEC;
+  int bt = ((nvec + 31) / 32) * 32;
+  bt = bt < 32 ? 32 : (bt > 256 ? 256 : bt);
+  const size_t smem = rs::stage_smem_bytes((int64_t)chunk * sizeof(T));
+  unsigned int* err = device_error_ptr();
+  if (layer)
+    return rs::launch_staged(layer_norm_staged<T, VEC>, g.rows, bt, cs, smem, st, xp, wp, bp, yp, sg, eps, err);
+  return rs::launch_staged(rms_norm_staged<T, VEC>, g.rows, bt, cs, smem, st, xp, wp, yp, sg, eps, err);
 }
 
 int run_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTensor* b,

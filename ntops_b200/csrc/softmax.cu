@@ -2,14 +2,14 @@
 //
 // Reference algorithm (ntops kernels/softmax.py:14-29): pass 1 keeps a running maximum and a
 // denominator rescaled by exp(prev_max - curr_max); pass 2 writes exp(x - max) / denominator.
-// Here a row along the last dimension is held in registers (rowreduce.cuh): the maximum is
-// reduced first, exp(x - max) is computed once per element and kept, its sum reduced, and
-// y = e * (1 / sum) is written — one HBM read, one write, one exp per element.  Statistics run
-// in fp32 (fp64 when the input or output is fp64), like torch's accumulate type, for every
-// output dtype.  A non-last `dim` uses a column kernel over the [outer, L, inner] view in
-// which each thread owns one (outer, inner) column and consecutive threads read consecutive
-// addresses.
-#include "rowreduce.cuh"
+// Here a row along the last dimension is staged in shared memory by a bulk copy (rowstage.cuh):
+// every thread forms its own maximum m and sum of exp(x - m); the (m, sum) pairs merge in ONE
+// reduction (sum' = sum * exp(m - M)), and y = exp(x - M) / S is written — one HBM read, one
+// write.  Statistics run in fp32 (fp64 when the input or output is fp64), like torch's
+// accumulate type, for every output dtype.  A non-last `dim` uses a column kernel over the
+// [outer, L, inner] view in which each thread owns one (outer, inner) column and consecutive
+// threads read consecutive addresses.
+#include "rowstage.cuh"
 
 namespace ntb {
 namespace {
@@ -19,51 +19,47 @@ template <typename TO> struct SAcc<double, TO> { using type = double; };
 template <typename TI> struct SAcc<TI, double> { using type = double; };
 template <> struct SAcc<double, double> { using type = double; };
 
-template <typename TI, typename TO, int VEC, int NCH>
-__global__ void __launch_bounds__(256) softmax_rows(const TI* __restrict__ x, TO* __restrict__ y, rr::RowGeom g) {
+template <typename TI, typename TO, int VEC>
+__global__ void __launch_bounds__(256) softmax_staged(const TI* __restrict__ x, TO* __restrict__ y, rs::StageGeom g,
+                                                      unsigned int* err) {
+  extern __shared__ __align__(128) uint8_t dyn[];
   using C = typename SAcc<TI, TO>::type;
-  __shared__ C red[32];
-  __shared__ C slots[2];
-  const int cs = g.cs;
-  const int rank = (int)(blockIdx.x % cs);
-  const int64_t row = blockIdx.x / cs;
-  const int64_t vecs = g.cols / VEC;
-  const int64_t base = (int64_t)rank * blockDim.x * NCH;
-  C xr[NCH][VEC];
-  bool valid[NCH];
-  rr::load_row<TI, C, VEC, NCH>(x + row * g.x_rs, vecs, base, xr, valid);
-  C m = rr::neg_inf<C>();
+  using R = rr::MaxSum<C>;
+  using VI = ew::Vec<TI, VEC>;
+  using VO = ew::Vec<TO, VEC>;
+  __shared__ R red[32];
+  __shared__ R slot;
+  bool pending = false;
+  rs::staged_rows<TI>(x, g, dyn, err, [&](int64_t row, const TI* sx, int64_t n, int64_t base) {
+    const int64_t nv = n / VEC;
+    // This thread's max (fmax skips NaN; a NaN still poisons the row through its exp in the
+    // sum) and sum of exp(x - max).
+    C m = rr::neg_inf<C>();
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
+      const VI xv = reinterpret_cast<const VI*>(sx)[v];
 #pragma unroll
-  for (int k = 0; k < NCH; ++k) {
-    if (!valid[k]) continue;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) m = rr::MaxOp{}(m, xr[k][e]);
-  }
-  m = rr::row_allreduce(m, rr::MaxOp{}, red, slots, 0, cs);
-  // A row of -inf gives exp(-inf - -inf) = NaN, as torch does.
-  C s = 0;
-#pragma unroll
-  for (int k = 0; k < NCH; ++k) {
-    if (!valid[k]) continue;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      xr[k][e] = rr::c_exp<C>(xr[k][e] - m);
-      s += xr[k][e];
+      for (int e = 0; e < VEC; ++e) m = fmax(m, cvt<C>(xv.v[e]));
     }
-  }
-  s = rr::row_allreduce(s, rr::SumOp{}, red, slots, 1, cs);
-  const C inv = C(1) / s;
-  TO* yrow = y + row * g.y_rs;
+    const C mref = m == rr::neg_inf<C>() ? C(0) : m;
+    C s[2] = {C(0), C(0)};
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
+      const VI xv = reinterpret_cast<const VI*>(sx)[v];
 #pragma unroll
-  for (int k = 0; k < NCH; ++k) {
-    if (!valid[k]) continue;
-    int64_t v = base + (int64_t)k * blockDim.x + threadIdx.x;
-    ew::Vec<TO, VEC> out;
+      for (int e = 0; e < VEC; ++e) s[e & 1] += rr::c_exp<C>(cvt<C>(xv.v[e]) - mref);
+    }
+    const R tot = rr::row_allreduce(R{m, s[0] + s[1]}, red, &slot, g.cs, pending);
+    // y = exp(x - M) / S; a row of -inf gives exp(NaN) = NaN, as torch does.
+    const C inv = C(1) / tot.s;
+    VO* yrow = reinterpret_cast<VO*>(y + row * g.y_rs + base);
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
+      const VI xv = reinterpret_cast<const VI*>(sx)[v];
+      VO out;
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) out.v[e] = cvt<TO>(xr[k][e] * inv);
-    ew::store_cs(reinterpret_cast<ew::Vec<TO, VEC>*>(yrow) + v, out);
-  }
-  rr::cluster_exit_barrier(cs);
+      for (int e = 0; e < VEC; ++e) out.v[e] = cvt<TO>(rr::c_exp<C>(cvt<C>(xv.v[e]) - tot.m) * inv);
+      ew::store_cs(yrow + v, out);
+    }
+  });
+  rr::cluster_exit(g.cs, pending);
 }
 
 // Long rows: three strided passes (max, sum, write); passes 2 and 3 re-read from L2.
@@ -71,18 +67,17 @@ template <typename TI, typename TO>
 __global__ void __launch_bounds__(1024) softmax_rows_looped(const TI* __restrict__ x, TO* __restrict__ y,
                                                             rr::RowGeom g) {
   using C = typename SAcc<TI, TO>::type;
-  __shared__ C red[32];
+  __shared__ rr::MaxSum<C> red[32];
   for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x) {
     const TI* xrow = x + row * g.x_rs;
-    C m = rr::neg_inf<C>();
-    for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x) m = rr::MaxOp{}(m, cvt<C>(xrow[i]));
-    m = rr::block_allreduce(m, rr::MaxOp{}, red);
-    C s = 0;
-    for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x) s += rr::c_exp<C>(cvt<C>(xrow[i]) - m);
-    const C inv = C(1) / rr::block_allreduce(s, rr::SumOp{}, red);
+    rr::MaxSum<C> acc = rr::MaxSum<C>::identity();
+    for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x)
+      acc = rr::MaxSum<C>::combine(acc, rr::MaxSum<C>{cvt<C>(xrow[i]), C(1)});
+    acc = rr::block_allreduce(acc, red);
+    const C inv = C(1) / acc.s;
     TO* yrow = y + row * g.y_rs;
     for (int64_t i = threadIdx.x; i < g.cols; i += blockDim.x)
-      yrow[i] = cvt<TO>(rr::c_exp<C>(cvt<C>(xrow[i]) - m) * inv);
+      yrow[i] = cvt<TO>(rr::c_exp<C>(cvt<C>(xrow[i]) - acc.m) * inv);
   }
 }
 
@@ -98,7 +93,7 @@ __global__ void __launch_bounds__(256) softmax_cols(const TI* __restrict__ x, TO
     const TI* xc = x + o * len * inner + i;
     TO* yc = y + o * len * inner + i;
     C m = rr::neg_inf<C>();
-    for (int64_t l = 0; l < len; ++l) m = rr::MaxOp{}(m, cvt<C>(xc[l * inner]));
+    for (int64_t l = 0; l < len; ++l) m = rr::nan_max(m, cvt<C>(xc[l * inner]));
     C s = 0;
     for (int64_t l = 0; l < len; ++l) s += rr::c_exp<C>(cvt<C>(xc[l * inner]) - m);
     const C inv = C(1) / s;
@@ -108,22 +103,20 @@ __global__ void __launch_bounds__(256) softmax_cols(const TI* __restrict__ x, TO
 
 template <typename TI, typename TO, int VEC>
 int launch_rows_softmax(const TI* x, TO* y, rr::RowGeom g, cudaStream_t st) {
-  int bt, nch, cs;
-  if (!rr::plan_row(g.cols / VEC, &bt, &nch, &cs)) {
+  int chunk = 0, cs = 1;
+  if (VEC == 1 || !rs::plan_stage(g.cols, (int)sizeof(TI), VEC, &chunk, &cs) ||
+      !rs::stage_aligned(x, g.x_rs, g.rows, (int)sizeof(TI))) {
     int grid = (int)(g.rows < (int64_t)sm_count() * 8 ? g.rows : (int64_t)sm_count() * 8);
     softmax_rows_looped<TI, TO><<<grid, 512, 0, st>>>(x, y, g);
     NTB_LAUNCH_CHECK();
     return NTB_OK;
   }
-  g.cs = cs;
-  switch (nch) {
-    case 1: return rr::launch_rows(softmax_rows<TI, TO, VEC, 1>, g.rows, bt, cs, st, x, y, g);
-    case 2: return rr::launch_rows(softmax_rows<TI, TO, VEC, 2>, g.rows, bt, cs, st, x, y, g);
-    case 4: return rr::launch_rows(softmax_rows<TI, TO, VEC, 4>, g.rows, bt, cs, st, x, y, g);
-    case 8: return rr::launch_rows(softmax_rows<TI, TO, VEC, 8>, g.rows, bt, cs, st, x, y, g);
-  }
-  set_error("internal: bad row plan");
-  return NTB_ERR_INVALID;
+  rs::StageGeom sg{g.rows, g.cols, g.x_rs, g.y_rs, cs, chunk};
+  const int nvec = chunk / VEC;
+  int bt = ((nvec + 31) / 32) * 32;
+  bt = bt < 32 ? 32 : (bt > 256 ? 256 : bt);
+  const size_t smem = rs::stage_smem_bytes((int64_t)chunk * sizeof(TI));
+  return rs::launch_staged(softmax_staged<TI, TO, VEC>, g.rows, bt, cs, smem, st, x, y, sg, device_error_ptr());
 }
 
 template <typename TI, typename TO>

@@ -9,24 +9,30 @@ from ntops_b200.torch.bitwise_not import bitwise_not
 from ntops_b200.torch.bitwise_or import bitwise_or
 from ntops_b200.torch.bmm import bmm
 from ntops_b200.torch.clamp import clamp
+from ntops_b200.torch.copysign import copysign
 from ntops_b200.torch.cos import cos
 from ntops_b200.torch.div import div
 from ntops_b200.torch.eq import eq
 from ntops_b200.torch.exp import exp
+from ntops_b200.torch.frac import frac
 from ntops_b200.torch.ge import ge
 from ntops_b200.torch.gelu import gelu
 from ntops_b200.torch.gt import gt
 from ntops_b200.torch.isinf import isinf
 from ntops_b200.torch.isnan import isnan
 from ntops_b200.torch.layer_norm import layer_norm
+from ntops_b200.torch.lcm import lcm
 from ntops_b200.torch.le import le
+from ntops_b200.torch.lgamma import lgamma
 from ntops_b200.torch.lt import lt
 from ntops_b200.torch.matmul import matmul
 from ntops_b200.torch.mm import mm
 from ntops_b200.torch.mul import mul
 from ntops_b200.torch.ne import ne
 from ntops_b200.torch.neg import neg
+from ntops_b200.torch.nextafter import nextafter
 from ntops_b200.torch.pow import pow
+from ntops_b200.torch.rad2deg import rad2deg
 from ntops_b200.torch.relu import relu
 from ntops_b200.torch.rms_norm import rms_norm
 from ntops_b200.torch.rotary_position_embedding import rotary_position_embedding
@@ -48,24 +54,30 @@ __all__ = [
     "bitwise_or",
     "bmm",
     "clamp",
+    "copysign",
     "cos",
     "div",
     "eq",
     "exp",
+    "frac",
     "ge",
     "gelu",
     "gt",
     "isinf",
     "isnan",
     "layer_norm",
+    "lcm",
     "le",
+    "lgamma",
     "lt",
     "matmul",
     "mm",
     "mul",
     "ne",
     "neg",
+    "nextafter",
     "pow",
+    "rad2deg",
     "relu",
     "rms_norm",
     "rotary_position_embedding",

@@ -88,6 +88,25 @@ def scaled_dot_product_attention(
         raise RuntimeError("scaled_dot_product_attention: query, key and value must share one dtype")
     qd, kd, vd, od = (_lib.describe(t) for t in (q, k, v, output))
     md = _lib.describe(mask) if mask is not None else None
+    sq, group = q.shape[-2], q.shape[-3] // k.shape[-3]
+    if sq <= _DECODE_MAX_Q and sq * group <= _DECODE_MAX_ROWS and q.dtype != torch.float64 \
+            and all(t.stride(-1) == 1 for t in (q, k, v)):
+        # Short query blocks (decoding against a KV cache): key-split kernel with a workspace
+        # for the per-chunk partial results, allocated here by the caller side.
+        nbytes = ctypes.c_int64(0)
+        launch_ok = lib().ntb_sdpa_decode_workspace(ctypes.byref(qd), ctypes.byref(kd), ctypes.byref(vd),
+                                                   ctypes.byref(nbytes))
+        _lib.check(launch_ok, "scaled_dot_product_attention")
+        ws = torch.empty(max(nbytes.value, 16), dtype=torch.uint8, device=q.device)
+        launch("scaled_dot_product_attention", lib().ntb_sdpa_decode, ctypes.byref(qd), ctypes.byref(kd),
+               ctypes.byref(vd), _lib.ref(md), ctypes.byref(od), float(scale), causal,
+               ctypes.c_void_p(ws.data_ptr()), nbytes.value, device_tensor=output)
+        return output
     launch("scaled_dot_product_attention", lib().ntb_sdpa, ctypes.byref(qd), ctypes.byref(kd),
            ctypes.byref(vd), _lib.ref(md), ctypes.byref(od), float(scale), causal, device_tensor=output)
     return output
+
+
+# Query blocks up to this many rows (and GQA group x rows) take the key-split decode kernel.
+_DECODE_MAX_Q = 16
+_DECODE_MAX_ROWS = 64

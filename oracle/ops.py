@@ -375,3 +375,53 @@ def scaled_dot_product_attention(query, key, value, attn_mask=None, is_causal=Fa
         lse = lse * alpha + p.sum(-1)
         mx = nxt
     return (acc / lse[..., None]).to(value.dtype)
+
+
+# --------------------------------------------------------- special elementwise (§ f2) -----
+def copysign(input, other):
+    """kernels/copysign.py:13-53: magnitude bits of input with the sign bit of other."""
+    a, b, dt = _promote(input, other)
+    out_dt = dt if dt.is_floating_point else torch.get_default_dtype()
+    return torch.copysign(_f(a), _f(b)).to(out_dt)
+
+
+def nextafter(input, other):
+    """kernels/nextafter.py:13-123: one step of the IEEE encoding from input toward other
+    (other itself when equal, NaN when either is NaN, the smallest subnormal from zero)."""
+    a, b, dt = _promote(input, other)
+    if dt in (torch.float32, torch.float64):
+        return torch.nextafter(a, b)
+    ia = a.contiguous().view(torch.int16).to(torch.int32) & 0xFFFF
+    ib = b.contiguous().view(torch.int16).to(torch.int32) & 0xFFFF
+    fa, fb = a.double(), b.double()
+    step_up = ia + 1
+    step_dn = ia - 1
+    away = (fa < fb) == ((ia & 0x8000) == 0)
+    r = torch.where(away, step_up, step_dn)
+    r = torch.where((ia & 0x7FFF) == 0, (ib & 0x8000) | 1, r)
+    r = torch.where(fa == fb, ib, r)
+    out = (r & 0xFFFF).to(torch.int32)
+    out = torch.where(out >= 0x8000, out - 0x10000, out).to(torch.int16).view(dt)
+    nan = torch.isnan(fa) | torch.isnan(fb)
+    return torch.where(nan, torch.tensor(float("nan"), dtype=dt), out)
+
+
+def lcm(input, other):
+    """kernels/lcm.py:14-128: |a / gcd(a, b) * b|, 0 when either is 0."""
+    a, b, _ = _promote(input, other)
+    return torch.lcm(a, b)
+
+
+def rad2deg(input):
+    """kernels/rad2deg.py:13-19: x * 180 / pi."""
+    return _unary_float(lambda x: x * (180.0 / math.pi), input)
+
+
+def frac(input):
+    """kernels/frac.py:12-27: x - trunc(x)."""
+    return _unary_float(lambda x: x - torch.trunc(x), input)
+
+
+def lgamma(input):
+    """kernels/lgamma.py:14-29: log |gamma(x)|."""
+    return _unary_float(torch.lgamma, input)

@@ -1,0 +1,51 @@
+"""Parity of the fused SwiGLU projection and of the whole Llama layer chain (fused and
+unfused) against the CPU oracle, at a small token count."""
+
+import pytest
+import torch
+
+import oracle.chain as OC
+import oracle.ops as O
+from tests.utils import assert_close
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,k,n", [(256, 512, 384), (200, 256, 128), (1000, 1024, 640), (128, 4096, 1024)])
+def test_swiglu_linear(m, k, n, dtype):
+    from ntops_b200.fused import pack_swiglu_weight, swiglu_linear
+
+    x = torch.randn(m, k).to(dtype)
+    wg = (torch.randn(k, n) * 0.05).to(dtype)
+    wu = (torch.randn(k, n) * 0.05).to(dtype)
+    packed = pack_swiglu_weight(wg.to(DEV), wu.to(DEV))
+    ref_packed = torch.stack((wg.view(k, n // 128, 128), wu.view(k, n // 128, 128)), 2).reshape(k, 2 * n)
+    assert torch.equal(packed.cpu(), ref_packed)
+    got = swiglu_linear(x.to(DEV), packed)
+    g64 = x.double() @ wg.double()
+    u64 = x.double() @ wu.double()
+    want = (g64 / (1 + torch.exp(-g64)) * u64).to(dtype)
+    assert_close(got, want, tol=(2e-2, 2e-2))
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_layer_chain_small(fused):
+    from ntops_b200 import chain
+
+    B, S = 1, 256
+    wts = chain.LayerWeights(DEV, seed=3)
+    sin, cos = chain.rope_tables(S, DEV)
+    x = torch.randn((B, S, chain.HIDDEN), generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    got = chain.layer_forward(x.to(DEV), wts, sin, cos, fused=fused).cpu()
+    w_cpu = [t.cpu() for t in (wts.wq, wts.wk, wts.wv, wts.wo, wts.wg, wts.wu, wts.wd, wts.norm1, wts.norm2)]
+    want = OC.layer_forward(x, w_cpu, sin.cpu(), cos.cpu())
+    # bf16 intermediates are rounded at different points on both sides: compare with a
+    # relative-to-scale tolerance (the output is a sum over 14336 products).
+    scale = want.double().abs().mean().item()
+    err = (got.double() - want.double()).abs()
+    assert err.mean().item() < 0.02 * scale, (err.mean().item(), scale)
+    assert err.max().item() < 0.5 * want.double().abs().max().item()
+    assert torch.isfinite(got.float()).all()

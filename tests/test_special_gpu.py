@@ -1,0 +1,59 @@
+"""Parity of the special-math elementwise operators (copysign, nextafter, lcm, rad2deg, frac,
+lgamma) against the oracle; nextafter and copysign are bit-exact, lcm is exact."""
+
+import pytest
+import torch
+
+import oracle.ops as O
+from tests.utils import assert_close, case_id, float_cases
+
+pytestmark = pytest.mark.gpu
+
+nt = pytest.importorskip("ntops_b200.torch") if torch.cuda.is_available() else None
+DEV = "cuda"
+CASES = float_cases((torch.float32, torch.float16, torch.bfloat16, torch.float64))
+
+
+@pytest.mark.parametrize("case", CASES, ids=case_id)
+def test_copysign_bit_exact(case):
+    shape, dtype = case
+    a, b = torch.randn(shape).to(dtype), torch.randn(shape).to(dtype)
+    b.view(-1)[::5] = -0.0
+    assert torch.equal(nt.copysign(a.to(DEV), b.to(DEV)).cpu(), O.copysign(a, b))
+
+
+@pytest.mark.parametrize("case", CASES, ids=case_id)
+def test_nextafter_bit_exact(case):
+    shape, dtype = case
+    a, b = torch.randn(shape).to(dtype), torch.randn(shape).to(dtype)
+    fa = a.view(-1)
+    fa[::7] = 0.0
+    b.view(-1)[::11] = a.view(-1)[::11]
+    got = nt.nextafter(a.to(DEV), b.to(DEV)).cpu()
+    want = O.nextafter(a, b)
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("dtype", [torch.int8, torch.int16, torch.int32, torch.int64])
+def test_lcm_exact(dtype):
+    a = torch.randint(-60, 60, (3000,), dtype=dtype)
+    b = torch.randint(-60, 60, (3000,), dtype=dtype)
+    assert torch.equal(nt.lcm(a.to(DEV), b.to(DEV)).cpu(), O.lcm(a, b))
+
+
+@pytest.mark.parametrize("case", CASES, ids=case_id)
+def test_rad2deg_frac_lgamma(case):
+    shape, dtype = case
+    x = (torch.randn(shape) * 5).to(dtype)
+    assert_close(nt.rad2deg(x.to(DEV)), O.rad2deg(x))
+    assert_close(nt.frac(x.to(DEV)), O.frac(x))
+    xp = (torch.rand(shape) * 10 + 0.1).to(dtype)
+    got = nt.lgamma(xp.to(DEV))
+    want = O.lgamma(xp)
+    tol = {torch.float32: (1e-5, 1e-5), torch.float64: (1e-10, 1e-10)}.get(dtype)
+    assert_close(got, want, tol=tol)
+
+
+def test_rad2deg_int_promotes():
+    i = torch.arange(-10, 10, dtype=torch.int32)
+    assert_close(nt.rad2deg(i.to(DEV)), O.rad2deg(i))
