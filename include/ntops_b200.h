@@ -224,6 +224,20 @@ NTB_API int ntb_sdpa_decode(const NtbTensor* q, const NtbTensor* k, const NtbTen
                             const NtbTensor* o, double scale, int causal_variant, void* workspace,
                             int64_t workspace_bytes, void* stream);
 
+/* ntb_sdpa_decode without a workspace argument, for callers that cannot allocate device
+ * memory when they run attention (all of HBM already reserved by their own pools, memory that
+ * only another allocator hands out, or a foreign-language binding that can pass the tensors it
+ * owns but cannot obtain scratch).  The per-chunk partial results live in a fixed 4 MiB device
+ * array inside the library, which every GPU that loads the library holds until exit; shapes that
+ * need more scratch (ntb_sdpa_decode_workspace() > 4 MiB) are refused with NTB_ERR_UNSUPPORTED.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race.  Allocates nothing (no cudaMalloc / cudaFree).
+ * This entry point has no counterpart in the reference. */
+NTB_API int ntb_sdpa_decode_static(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v,
+                                   const NtbTensor* mask, const NtbTensor* o, double scale, int causal_variant,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,6 +60,7 @@ EXPORTS = (
     "ntb_sdpa",
     "ntb_sdpa_decode_workspace",
     "ntb_sdpa_decode",
+    "ntb_sdpa_decode_static",
 )
 
 
@@ -100,6 +101,7 @@ _SIGNATURES = {
         [_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP, ctypes.c_int64, _VP],
         ctypes.c_int,
     ),
+    "ntb_sdpa_decode_static": ([_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP], ctypes.c_int),
 }
 
 _lib = None

@@ -327,3 +327,63 @@ extern "C" int ntb_sdpa_decode(const NtbTensor* q, const NtbTensor* k, const Ntb
   a.ws = reinterpret_cast<float*>(workspace);
   return decode::launch(a, q->dtype, (cudaStream_t)stream);
 }
+
+// ----------------------------------------------------- entry point without allocation ----
+// Some callers cannot allocate device memory at the moment they run attention: a serving
+// runtime that reserved all of HBM for its own pools at start-up and forbids further
+// cudaMalloc, a host whose only device memory is what another framework's allocator hands it,
+// or a foreign-language binding that can pass pointers to the tensors it owns but has no way to
+// obtain a workspace.  ntb_sdpa_decode_static serves them: it is ntb_sdpa_decode with its
+// per-chunk partial results kept in the fixed device array below instead of a caller workspace.
+namespace ntb {
+namespace decode {
+
+// 4 MiB, enough for e.g. batch 8 x 32 query heads x 16 query rows x 6 key chunks at head_dim 128.
+constexpr int64_t kStaticScratchBytes = 4ll << 20;
+
+// Every GPU that loads this library holds this array until the process exits.  All calls on a
+// device share it and each call leaves its partial results behind; every call writes all of the
+// scratch it reads before reading it, so nothing needs clearing, but calls that overlap on the
+// GPU (different streams, or different host threads) overwrite each other's partials and race.
+static __device__ __align__(256) float g_static_scratch[kStaticScratchBytes / sizeof(float)];
+
+// Device address of g_static_scratch on the current device.  In host code the array's name only
+// stands in for the device copy, so the address is asked of the runtime once per device (with
+// that device current) and cached.
+int static_scratch(float** out) {
+  static std::mutex mu;
+  static float* cache[64] = {nullptr};
+  int dev = 0;
+  NTB_CUDA(cudaGetDevice(&dev));
+  NTB_ARG(dev >= 0 && dev < 64, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    NTB_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+    cache[dev] = reinterpret_cast<float*>(p);
+  }
+  *out = cache[dev];
+  return NTB_OK;
+}
+
+}  // namespace decode
+}  // namespace ntb
+
+extern "C" int ntb_sdpa_decode_static(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v,
+                                      const NtbTensor* mask, const NtbTensor* o, double scale, int causal_variant,
+                                      void* stream) {
+  using namespace ntb;
+  NTB_ARG(o != nullptr, "output is NULL");
+  decode::Args a;
+  int rc = decode::plan(q, k, v, o, mask, scale, causal_variant, &a);
+  if (rc != NTB_OK) return rc;
+  const int64_t need = decode::ws_floats(a) * (int64_t)sizeof(float);
+  NTB_UNSUP(need <= decode::kStaticScratchBytes,
+            "these shapes need %lld bytes of scratch; the static scratch holds %lld bytes "
+            "(use ntb_sdpa_decode with a workspace)",
+            (long long)need, (long long)decode::kStaticScratchBytes);
+  float* scratch = nullptr;
+  if ((rc = decode::static_scratch(&scratch)) != NTB_OK) return rc;
+  a.ws = scratch;
+  return decode::launch(a, q->dtype, (cudaStream_t)stream);
+}
