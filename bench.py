@@ -59,11 +59,11 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback (profiling recipe)"
 
 
-def config(world):
+def config(world, global_batch=GLOBAL_BATCH):
     return {
         "workload": "llama3_8b_layer_chain (BASELINE config 3): rms_norm, q/k/v mm, rope, causal GQA sdpa, "
         "o mm, residual add, rms_norm, gate/up mm, silu*mul, down mm",
-        "global_batch": GLOBAL_BATCH,
+        "global_batch": global_batch,
         "seq_len": SEQ,
         "parallelism": f"dp{world} (sequences sharded, no data-path collective)",
         "l2": "inputs larger than L2 (x 268 MB + weights 436 MB per pass)",
@@ -376,6 +376,10 @@ def main():
     ap.add_argument("--impl", default="ntops_b200", choices=["ntops_b200", "reference"])
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op table")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH,
+                    help="sequences of 2048 tokens over all ranks (the BASELINE config is 16)")
+    ap.add_argument("--no-graph", action="store_true", help="launch every operator from Python each step "
+                    "instead of replaying the step as one CUDA graph")
     ap.add_argument("--case", default=None, help="run one operator case (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=2)
     args = ap.parse_args()
@@ -401,7 +405,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     peaks, peak_src = load_peaks()
 
-    s0, s1 = shard_range(GLOBAL_BATCH, rank, world)
+    global_batch = args.global_batch
+    s0, s1 = shard_range(global_batch, rank, world)
     batch = s1 - s0
     tokens = batch * SEQ
     wts = chain.LayerWeights(dev)
@@ -413,8 +418,6 @@ def main():
     for _ in range(args.warmup):
         chain.layer_forward(x, wts, sin, cos)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
 
     gemm_events = []
 
@@ -426,19 +429,61 @@ def main():
         gemm_events.append((s, e))
         return out
 
+    # One layer pass as a CUDA graph (the step's kernels with no host launch gaps); the GEMM
+    # timing events are recorded inside the captured pass, so they replay with it.
+    use_graph = not args.no_graph
+    graph = None
+    step_launches = 0
+    if use_graph:
+        cap_events = []
+
+        def cap_hook(fn, a, b):
+            # external events become real event-record nodes of the graph (timestamps on replay)
+            s = torch.cuda.Event(enable_timing=True, external=True)
+            e = torch.cuda.Event(enable_timing=True, external=True)
+            s.record()
+            out = fn(a, b)
+            e.record()
+            cap_events.append((s, e))
+            return out
+
+        chain.layer_forward(x, wts, sin, cos, mm_hook=cap_hook)  # warm caches / attributes once more
+        torch.cuda.synchronize()
+        cap_events.clear()
+        graph = torch.cuda.CUDAGraph()
+        l0 = ntu.launch_count
+        with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+            y_static = chain.layer_forward(x, wts, sin, cos, mm_hook=cap_hook)
+        step_launches = ntu.launch_count - l0
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
     # ---- timed region: inputs resident in HBM
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = ntu.launch_count
+    gemm_times = []
     with ClockSampler(local_rank) as clk:
         torch.cuda.synchronize()
         start.record()
         for _ in range(args.steps):
-            y = chain.layer_forward(x, wts, sin, cos, mm_hook=mm_hook)
+            if graph is not None:
+                graph.replay()
+            else:
+                y = chain.layer_forward(x, wts, sin, cos, mm_hook=mm_hook)
         end.record()
         torch.cuda.synchronize()
-    launches = ntu.launch_count - launches0
+    if graph is not None:
+        y = y_static
+        launches = step_launches * args.steps
+        # the captured events hold the last replay's GEMM times: one pass's worth per step
+        gemm_times = [s.elapsed_time(e) for s, e in cap_events] * args.steps
+    else:
+        launches = ntu.launch_count - launches0
+        gemm_times = [s.elapsed_time(e) for s, e in gemm_events]
     ms_local = start.elapsed_time(end)
-    gemm_times = [s.elapsed_time(e) for s, e in gemm_events]
     gemm_ms = sum(gemm_times)
     # the fused gate/up (SwiGLU) projection is the 5th of the 6 launches of a pass
     shapes = chain.gemm_shapes(tokens)
@@ -446,7 +491,7 @@ def main():
     gm, gn, gk = shapes[4]
     gate_tflops = 2 * gm * gn * gk / (gate_ms * 1e-3) / 1e12
     ms = max_over_ranks(ms_local, dev)
-    value = GLOBAL_BATCH * SEQ * args.steps / (ms * 1e-3)
+    value = global_batch * SEQ * args.steps / (ms * 1e-3)
     gemm_tflops = mm_flops * args.steps / (gemm_ms * 1e-3) / 1e12
     rc = _lib.load().ntb_check_device_error(None)
     assert rc == 0, "a kernel reported a device-side timeout"
@@ -500,7 +545,7 @@ def main():
     e2.record(comp)
     torch.cuda.synchronize()
     ms_e2e = max_over_ranks(s2.elapsed_time(e2), dev)
-    e2e_value = GLOBAL_BATCH * SEQ * args.steps / (ms_e2e * 1e-3)
+    e2e_value = global_batch * SEQ * args.steps / (ms_e2e * 1e-3)
     assert torch.equal(yh[(args.steps - 1) & 1], y.cpu()), "end-to-end output differs from the resident run"
 
     ops = None
@@ -530,7 +575,7 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded randn inputs, random-init weights ~N(0,0.02))",
-            "config": config(world),
+            "config": config(world, global_batch),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": x.numel() * 2 * world,
                     "d2h_bytes_per_step": y.numel() * 2 * world},
             "gpu_launches": launches * world,
@@ -540,13 +585,15 @@ def main():
                          "achieved": gate_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                          "frac": gate_tflops / peaks["bf16_tflops_sustained"],
                          "traffic": SWIGLU_GEMM_TRAFFIC if batch == GLOBAL_BATCH else None,
+                         "traffic_note": "measured at the full one-GPU size (16 x 2048 tokens)",
                          "traffic_algorithmic": (gm * gk + gk * gn + gm * gn // 2) * 2,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
                                            "shape (profiles/gemm_tc_kernel-swiglu_32768x28672x4096_bf16.md)",
                          "peak_source": f"bf16_tflops_sustained, {peak_src}",
                          "all_gemms": {"achieved": gemm_tflops, "frac": gemm_tflops / peaks["bf16_tflops_sustained"],
                                        "share_of_step": gemm_ms / ms_local}},
-            "step_tflops": (mm_flops + attn_flops) * GLOBAL_BATCH / batch / (ms / args.steps * 1e-3) / 1e12,
+            "step_tflops": (mm_flops + attn_flops) * global_batch / batch / (ms / args.steps * 1e-3) / 1e12,
+            "cuda_graph": use_graph,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "ops": ops,

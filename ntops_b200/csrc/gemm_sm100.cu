@@ -22,6 +22,7 @@
 // 16-bit types; TF32 takes K-major operands.  Shapes or strides that TMA cannot address
 // (unaligned rows) and IEEE fp32 / fp64 run on the CUDA-core kernel at the end of this file.
 #include <atomic>
+#include <cmath>
 #include <type_traits>
 
 #include "elementwise.cuh"
@@ -593,7 +594,19 @@ extern "C" int ntb_gemm(const NtbTensor* a, const NtbTensor* bm, const NtbTensor
     }
   }
   if (use_tc) {
-    const bool wide = p.N > 128;
+    // Tile width: a 128 x 128 tile reads 64 FLOP per shared-memory byte, which saturates the SM's
+    // shared-memory bandwidth before the tensor core (measured ~0.68 of the 128 x 256 tile's
+    // throughput); 128 x 128 tiles only pay when they fix a badly quantised last wave.  Pick the
+    // width with the better estimated efficiency = wave occupancy x relative tile efficiency.
+    bool wide = p.N > 128;
+    if (wide) {
+      const double sms = (double)sm_count();
+      const int64_t mb = (p.M + BM - 1) / BM;
+      const int64_t t256 = mb * ((p.N + 255) / 256) * p.batch, t128 = mb * ((p.N + 127) / 128) * p.batch;
+      const double e256 = (double)t256 / (std::ceil((double)t256 / sms) * sms);
+      const double e128 = 0.68 * (double)t128 / (std::ceil((double)t128 / sms) * sms);
+      wide = e256 >= e128;
+    }
     switch (a->dtype) {
       case NTB_BF16:
         return wide ? launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st)
