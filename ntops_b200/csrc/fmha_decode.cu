@@ -38,7 +38,8 @@ __host__ __device__ inline int64_t ws_floats(const Args& a) {
   return (int64_t)a.B * a.Hq * a.Sq * a.splits * (a.Dv + 2);
 }
 
-template <typename T>
+// RPW: query rows per warp (rows r = warp, warp + 4, ...); DC: output columns per lane / 32.
+template <typename T, int RPW, int DC>
 __global__ void __launch_bounds__(kThreads) decode_partial(Args a) {
   extern __shared__ __align__(16) float sm[];
   const int D = a.D, Dv = a.Dv;
@@ -60,14 +61,14 @@ __global__ void __launch_bounds__(kThreads) decode_partial(Args a) {
   }
   const int off = a.causal == 2 ? a.Skv - a.Sq : 0;
   // Per-row state of this warp's rows r = warp, warp + 4, ...
-  constexpr int kRowsPerWarp = kMaxRows / 4;
-  float m[kRowsPerWarp], l[kRowsPerWarp], acc[kRowsPerWarp][kMaxD / 32];
+  constexpr int kRowsPerWarp = RPW;
+  float m[kRowsPerWarp], l[kRowsPerWarp], acc[kRowsPerWarp][DC];
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i) {
     m[i] = -INFINITY;
     l[i] = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxD / 32; ++c) acc[i][c] = 0.f;
+    for (int c = 0; c < DC; ++c) acc[i][c] = 0.f;
   }
   for (int k0 = k_begin; k0 < k_end; k0 += kKeys) {
     __syncthreads();
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(kThreads) decode_partial(Args a) {
       Ps[warp * kKeys + lane] = pj;
       __syncwarp();
 #pragma unroll
-      for (int c = 0; c < kMaxD / 32; ++c) {
+      for (int c = 0; c < DC; ++c) {
         const int d = lane + 32 * c;
         if (d < Dv) {
           float s2 = acc[i][c] * alpha;
@@ -150,7 +151,7 @@ __global__ void __launch_bounds__(kThreads) decode_partial(Args a) {
     const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
     float* w = a.ws + ((((int64_t)b * a.Hq + hq) * a.Sq + s) * a.splits + split) * (Dv + 2);
 #pragma unroll
-    for (int c = 0; c < kMaxD / 32; ++c) {
+    for (int c = 0; c < DC; ++c) {
       const int d = lane + 32 * c;
       if (d < Dv) w[d] = acc[i][c];
     }
@@ -231,10 +232,10 @@ int plan(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTe
             "attn_mask must be expanded to [B, Hq, Sq, Skv]");
     NTB_UNSUP(mask->dtype == q->dtype, "attn_mask dtype must equal the query dtype");
   }
-  // Split the key range so that (batch x kv heads x chunks) fills the GPU twice over, with
+  // Split the key range so that (batch x kv heads x chunks) fills the GPU four times over, with
   // chunks of at least 256 keys.
   const int64_t units = (int64_t)a->B * a->Hkv;
-  int splits = (int)((2 * sm_count() + units - 1) / units);
+  int splits = (int)((4 * sm_count() + units - 1) / units);
   const int max_splits = (a->Skv + 255) / 256;
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
@@ -271,15 +272,37 @@ int plan(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTe
   return NTB_OK;
 }
 
+template <typename T, int RPW, int DC>
+int launch_partial(const Args& a, size_t smem, cudaStream_t st) {
+  auto k1 = decode_partial<T, RPW, DC>;
+  if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k1<<<dim3(a.splits, a.Hkv, a.B), kThreads, smem, st>>>(a);
+  NTB_LAUNCH_CHECK();
+  return NTB_OK;
+}
+
+template <typename T, int RPW>
+int launch_dc(const Args& a, size_t smem, cudaStream_t st) {
+  const int dc = (a.Dv + 31) / 32;
+  if (dc <= 1) return launch_partial<T, RPW, 1>(a, smem, st);
+  if (dc <= 2) return launch_partial<T, RPW, 2>(a, smem, st);
+  if (dc <= 4) return launch_partial<T, RPW, 4>(a, smem, st);
+  return launch_partial<T, RPW, 8>(a, smem, st);
+}
+
 template <typename T>
 int launch_typed(const Args& a, cudaStream_t st) {
   const size_t smem = sizeof(float) * ((size_t)a.group * a.Sq * a.D + (size_t)kKeys * (a.D + 1) +
                                        (size_t)kKeys * (a.Dv + 1) + 4 * kKeys);
-  auto k1 = decode_partial<T>;
-  if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   NTB_UNSUP(a.Hkv <= 65535 && a.B <= 65535, "too many heads / batches");
-  k1<<<dim3(a.splits, a.Hkv, a.B), kThreads, smem, st>>>(a);
-  NTB_LAUNCH_CHECK();
+  const int rpw = (a.group * a.Sq + 3) / 4;  // query rows per warp
+  int rc;
+  if (rpw <= 1) rc = launch_dc<T, 1>(a, smem, st);
+  else if (rpw <= 2) rc = launch_dc<T, 2>(a, smem, st);
+  else if (rpw <= 4) rc = launch_dc<T, 4>(a, smem, st);
+  else if (rpw <= 8) rc = launch_dc<T, 8>(a, smem, st);
+  else rc = launch_dc<T, 16>(a, smem, st);
+  if (rc != NTB_OK) return rc;
   const int64_t rows = (int64_t)a.B * a.Hq * a.Sq;
   NTB_UNSUP(rows <= 0x7fffffffLL, "too many rows");
   decode_merge<T><<<(unsigned)rows, kThreads, 0, st>>>(a);

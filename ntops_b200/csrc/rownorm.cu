@@ -3,8 +3,8 @@
 // Reference algorithm (ntops): kernels/rms_norm.py:10-20 — fp32 sum of squares over the row,
 // rms = sqrt(sum / n + eps), y = x / rms * w; kernels/layer_norm.py:11-31 — fp32 mean, biased
 // variance of (x - mean), y = (x - mean) / sqrt(var + eps) * w + b.  Both read each row once
-// from HBM here (a bulk copy stages it in shared memory, see rowstage.cuh) and reduces once;
-// the reference reads it 2 and 3 times.  Statistics are fp32 for half/bf16/fp32 inputs and fp64 for fp64.
+// from HBM here (bulk copies stream it through shared memory, see rowstage.cuh) and reduces
+// once; the reference reads it 2 and 3 times.  Statistics are fp32 for half/bf16/fp32 inputs and fp64 for fp64.
 #include "rowstage.cuh"
 
 namespace ntb {
@@ -15,46 +15,52 @@ template <> struct Acc<double> { using type = double; };
 
 // ------------------------------------------------------------------ RMSNorm ---------------
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) rms_norm_staged(const T* __restrict__ x, const T* __restrict__ w,
-                                                        T* __restrict__ y, rs::StageGeom g, double eps,
+__global__ void __launch_bounds__(256) rms_norm_stream(const T* __restrict__ x, const T* __restrict__ w,
+                                                        T* __restrict__ y, rs::StreamGeom g, double eps,
                                                         unsigned int* err) {
   extern __shared__ __align__(128) uint8_t dyn[];
   using C = typename Acc<T>::type;
   using R = rr::Sum<C>;
   using V = ew::Vec<T, VEC>;
   __shared__ R red[32];
-  __shared__ R slot;
-  bool pending = false;
-  rs::staged_rows<T>(x, g, dyn, err, [&](int64_t row, const T* sx, int64_t n, int64_t base) {
-    const int64_t nv = n / VEC;
-    C ss[2] = {C(0), C(0)};
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
-      const V xv = reinterpret_cast<const V*>(sx)[v];
+  C ss0, ss1, rinv;
+  rs::stream_rows<T>(
+      x, g, dyn, err, [&] { ss0 = ss1 = C(0); },
+      [&](const T* sx, int n, int) {
+        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
+          const V xv = reinterpret_cast<const V*>(sx)[v];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const C c = cvt<C>(xv.v[e]);
-        ss[e & 1] += c * c;
-      }
-    }
-    const C tot = rr::row_allreduce(R{ss[0] + ss[1]}, red, &slot, g.cs, pending).v;
-    const C rinv = C(1) / rr::c_sqrt<C>(tot / C(g.cols) + C(eps));
-    V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + base);
-    const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + base) : nullptr;
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
-      const V xv = reinterpret_cast<const V*>(sx)[v];
-      V out;
-      if (wrow != nullptr) {
-        const V wv = wrow[v];
+          for (int e = 0; e < VEC; e += 2) {
+            const C a = cvt<C>(xv.v[e]);
+            ss0 += a * a;
+            if (e + 1 < VEC) {
+              const C b = cvt<C>(xv.v[e + 1]);
+              ss1 += b * b;
+            }
+          }
+        }
+      },
+      [&] {
+        const C tot = rr::block_allreduce(R{ss0 + ss1}, red).v;
+        rinv = C(1) / rr::c_sqrt<C>(tot / C(g.cols) + C(eps));
+      },
+      [&](const T* sx, int n, int col0, int64_t row) {
+        V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + col0);
+        const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + col0) : nullptr;
+        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
+          const V xv = reinterpret_cast<const V*>(sx)[v];
+          V out;
+          if (wrow != nullptr) {
+            const V wv = wrow[v];
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(cvt<C>(xv.v[e]) * rinv * cvt<C>(wv.v[e]));
-      } else {
+            for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(cvt<C>(xv.v[e]) * rinv * cvt<C>(wv.v[e]));
+          } else {
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(cvt<C>(xv.v[e]) * rinv);
-      }
-      ew::store_cs(yrow + v, out);
-    }
-  });
-  rr::cluster_exit(g.cs, pending);
+            for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(cvt<C>(xv.v[e]) * rinv);
+          }
+          ew::store_cs(yrow + v, out);
+        }
+      });
 }
 
 // Rows too long for the register-resident kernel: strided passes, later ones from L2.
@@ -83,62 +89,73 @@ __global__ void __launch_bounds__(1024) rms_norm_looped(const T* __restrict__ x,
 }
 
 // ---------------------------------------------------------------- LayerNorm ---------------
-// One reduction: every thread forms the exact (count, mean, M2) of its own elements in two
-// passes over the staged row, and the triples merge across threads, warps and CTAs with Chan's
-// formula.
+// One reduction per row: every thread keeps the count, sum and sum of squares of its elements
+// shifted by the first value it saw (shifting keeps the single pass exact enough: the variance
+// of x - K equals that of x and K is within the data's spread), turns them into a
+// (count, mean, M2) triple, and the triples merge across the CTA with Chan's formula.
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) layer_norm_staged(const T* __restrict__ x, const T* __restrict__ w,
+__global__ void __launch_bounds__(256) layer_norm_stream(const T* __restrict__ x, const T* __restrict__ w,
                                                           const T* __restrict__ b, T* __restrict__ y,
-                                                          rs::StageGeom g, double eps, unsigned int* err) {
+                                                          rs::StreamGeom g, double eps, unsigned int* err) {
   extern __shared__ __align__(128) uint8_t dyn[];
   using C = typename Acc<T>::type;
   using R = rr::Welford<C>;
   using V = ew::Vec<T, VEC>;
   __shared__ R red[32];
-  __shared__ R slot;
-  bool pending = false;
-  rs::staged_rows<T>(x, g, dyn, err, [&](int64_t row, const T* sx, int64_t n, int64_t base) {
-    const int64_t nv = n / VEC;
-    C s[2] = {C(0), C(0)};
-    int cnt = 0;
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
-      const V xv = reinterpret_cast<const V*>(sx)[v];
-      cnt += VEC;
+  C shift, s, ss, mean, rstd;
+  int cnt;
+  bool have_shift;
+  rs::stream_rows<T>(
+      x, g, dyn, err,
+      [&] {
+        s = ss = C(0);
+        cnt = 0;
+        have_shift = false;
+        shift = C(0);
+      },
+      [&](const T* sx, int n, int) {
+        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
+          const V xv = reinterpret_cast<const V*>(sx)[v];
+          if (!have_shift) {
+            shift = cvt<C>(xv.v[0]);
+            have_shift = true;
+          }
+          cnt += VEC;
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) s[e & 1] += cvt<C>(xv.v[e]);
-    }
-    const C mean_t = cnt ? (s[0] + s[1]) / C(cnt) : C(0);
-    C m2[2] = {C(0), C(0)};
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
-      const V xv = reinterpret_cast<const V*>(sx)[v];
+          for (int e = 0; e < VEC; ++e) {
+            const C d = cvt<C>(xv.v[e]) - shift;
+            s += d;
+            ss += d * d;
+          }
+        }
+      },
+      [&] {
+        const C nt = C(cnt);
+        const C m_t = cnt ? s / nt : C(0);
+        const C m2_t = cnt ? ss - s * m_t : C(0);
+        const R st = rr::block_allreduce(R{nt, shift + m_t, m2_t > C(0) ? m2_t : C(0)}, red);
+        mean = st.mean;
+        rstd = C(1) / rr::c_sqrt<C>(st.m2 / C(g.cols) + C(eps));
+      },
+      [&](const T* sx, int n, int col0, int64_t row) {
+        V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + col0);
+        const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + col0) : nullptr;
+        const V* brow = b != nullptr ? reinterpret_cast<const V*>(b + col0) : nullptr;
+        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
+          const V xv = reinterpret_cast<const V*>(sx)[v];
+          V wv, bv, out;
+          if (wrow != nullptr) wv = wrow[v];
+          if (brow != nullptr) bv = brow[v];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const C d = cvt<C>(xv.v[e]) - mean_t;
-        m2[e & 1] += d * d;
-      }
-    }
-    const R st = rr::row_allreduce(R{C(cnt), mean_t, m2[0] + m2[1]}, red, &slot, g.cs, pending);
-    const C mean = st.mean;
-    const C rstd = C(1) / rr::c_sqrt<C>(st.m2 / C(g.cols) + C(eps));
-    V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + base);
-    const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + base) : nullptr;
-    const V* brow = b != nullptr ? reinterpret_cast<const V*>(b + base) : nullptr;
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
-      const V xv = reinterpret_cast<const V*>(sx)[v];
-      V wv, bv, out;
-      if (wrow != nullptr) wv = wrow[v];
-      if (brow != nullptr) bv = brow[v];
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        C r = (cvt<C>(xv.v[e]) - mean) * rstd;  // subtract first: no cancellation
-        if (wrow != nullptr) r *= cvt<C>(wv.v[e]);
-        if (brow != nullptr) r += cvt<C>(bv.v[e]);
-        out.v[e] = cvt<T>(r);
-      }
-      ew::store_cs(yrow + v, out);
-    }
-  });
-  rr::cluster_exit(g.cs, pending);
+          for (int e = 0; e < VEC; ++e) {
+            C r = (cvt<C>(xv.v[e]) - mean) * rstd;  // subtract first: no cancellation
+            if (wrow != nullptr) r *= cvt<C>(wv.v[e]);
+            if (brow != nullptr) r += cvt<C>(bv.v[e]);
+            out.v[e] = cvt<T>(r);
+          }
+          ew::store_cs(yrow + v, out);
+        }
+      });
 }
 
 template <typename T>
@@ -212,9 +229,9 @@ int launch_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTen
   const T* wp = w ? (const T*)w->data : nullptr;
   const T* bp = b ? (const T*)b->data : nullptr;
   T* yp = (T*)y->data;
-  int chunk = 0, cs = 1;
-  if (VEC == 1 || !rs::plan_stage(g.cols, (int)sizeof(T), VEC, &chunk, &cs) ||
-      !rs::stage_aligned(xp, g.x_rs, g.rows, (int)sizeof(T))) {
+  int chunk = 0, nc = 1;
+  if (VEC == 1 || !rs::plan_stream(g.cols, (int)sizeof(T), VEC, &chunk, &nc) ||
+      !rs::stream_aligned(xp, g.x_rs, g.rows, (int)sizeof(T))) {
     int grid = (int)(g.rows < (int64_t)sm_count() * 8 ? g.rows : (int64_t)sm_count() * 8);
     if (layer)
       layer_norm_looped<T><<<grid, 512, 0, st>>>(xp, wp, bp, yp, g, eps);
@@ -223,15 +240,17 @@ int launch_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTen
     NTB_LAUNCH_CHECK();
     return NTB_OK;
   }
-  rs::StageGeom sg{g.rows, g.cols, g.x_rs, g.y_rs, cs, chunk};
+  rs::StreamGeom sg{g.rows, g.cols, g.x_rs, g.y_rs, chunk, nc};
   const int nvec = chunk / VEC;
   int bt = ((nvec + 31) / 32) * 32;
   bt = bt < 32 ? 32 : (bt > 256 ? 256 : bt);
-  const size_t smem = rs::stage_smem_bytes((int64_t)chunk * sizeof(T));
+  const size_t smem = rs::stream_smem_bytes(chunk * (int)sizeof(T));
+  const int64_t row_bytes = g.cols * (int64_t)sizeof(T);
   unsigned int* err = device_error_ptr();
   if (layer)
-    return rs::launch_staged(layer_norm_staged<T, VEC>, g.rows, bt, cs, smem, st, xp, wp, bp, yp, sg, eps, err);
-  return rs::launch_staged(rms_norm_staged<T, VEC>, g.rows, bt, cs, smem, st, xp, wp, yp, sg, eps, err);
+    return rs::launch_stream(layer_norm_stream<T, VEC>, g.rows, row_bytes, nc, bt, smem, st, xp, wp, bp, yp, sg,
+                             eps, err);
+  return rs::launch_stream(rms_norm_stream<T, VEC>, g.rows, row_bytes, nc, bt, smem, st, xp, wp, yp, sg, eps, err);
 }
 
 int run_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTensor* b,

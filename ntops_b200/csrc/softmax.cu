@@ -2,13 +2,13 @@
 //
 // Reference algorithm (ntops kernels/softmax.py:14-29): pass 1 keeps a running maximum and a
 // denominator rescaled by exp(prev_max - curr_max); pass 2 writes exp(x - max) / denominator.
-// Here a row along the last dimension is staged in shared memory by a bulk copy (rowstage.cuh):
-// every thread forms its own maximum m and sum of exp(x - m); the (m, sum) pairs merge in ONE
-// reduction (sum' = sum * exp(m - M)), and y = exp(x - M) / S is written — one HBM read, one
-// write.  Statistics run in fp32 (fp64 when the input or output is fp64), like torch's
-// accumulate type, for every output dtype.  A non-last `dim` uses a column kernel over the
-// [outer, L, inner] view in which each thread owns one (outer, inner) column and consecutive
-// threads read consecutive addresses.
+// Here a row along the last dimension streams through shared memory in bulk-copied chunks
+// (rowstage.cuh): pass 0 keeps every thread's running (max, sum of exp(x - max)), the pairs
+// merge in ONE reduction (sum' = sum * exp(m - M)), and pass 1 writes y = exp(x - M) / S.  A row
+// of up to 16 KB is read from HBM once; longer rows are re-read for pass 1 from L2.  Statistics
+// run in fp32 (fp64 when the input or output is fp64), like torch's accumulate type, for every
+// output dtype.  A non-last `dim` uses a column kernel over the [outer, L, inner] view in which
+// each thread owns one (outer, inner) column and consecutive threads read consecutive addresses.
 #include "rowstage.cuh"
 
 namespace ntb {
@@ -20,7 +20,7 @@ template <typename TI> struct SAcc<TI, double> { using type = double; };
 template <> struct SAcc<double, double> { using type = double; };
 
 template <typename TI, typename TO, int VEC>
-__global__ void __launch_bounds__(256) softmax_staged(const TI* __restrict__ x, TO* __restrict__ y, rs::StageGeom g,
+__global__ void __launch_bounds__(256) softmax_stream(const TI* __restrict__ x, TO* __restrict__ y, rs::StreamGeom g,
                                                       unsigned int* err) {
   extern __shared__ __align__(128) uint8_t dyn[];
   using C = typename SAcc<TI, TO>::type;
@@ -28,38 +28,43 @@ __global__ void __launch_bounds__(256) softmax_staged(const TI* __restrict__ x, 
   using VI = ew::Vec<TI, VEC>;
   using VO = ew::Vec<TO, VEC>;
   __shared__ R red[32];
-  __shared__ R slot;
-  bool pending = false;
-  rs::staged_rows<TI>(x, g, dyn, err, [&](int64_t row, const TI* sx, int64_t n, int64_t base) {
-    const int64_t nv = n / VEC;
-    // This thread's max (fmax skips NaN; a NaN still poisons the row through its exp in the
-    // sum) and sum of exp(x - max).
-    C m = rr::neg_inf<C>();
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
-      const VI xv = reinterpret_cast<const VI*>(sx)[v];
+  C m, sum, M, inv;
+  rs::stream_rows<TI>(
+      x, g, dyn, err, [&] { m = rr::neg_inf<C>(), sum = C(0); },
+      [&](const TI* sx, int n, int) {
+        // running (max, sum of exp(x - max)) of this thread's elements; fmax skips NaN but a NaN
+        // still poisons the row through its exp in the sum
+        C cm = m;
+        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
+          const VI xv = reinterpret_cast<const VI*>(sx)[v];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) m = fmax(m, cvt<C>(xv.v[e]));
-    }
-    const C mref = m == rr::neg_inf<C>() ? C(0) : m;
-    C s[2] = {C(0), C(0)};
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
-      const VI xv = reinterpret_cast<const VI*>(sx)[v];
+          for (int e = 0; e < VEC; ++e) cm = fmax(cm, cvt<C>(xv.v[e]));
+        }
+        const C ref = cm == rr::neg_inf<C>() ? C(0) : cm;
+        C acc = (m == rr::neg_inf<C>()) ? C(0) : sum * rr::c_exp<C>(m - ref);
+        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
+          const VI xv = reinterpret_cast<const VI*>(sx)[v];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) s[e & 1] += rr::c_exp<C>(cvt<C>(xv.v[e]) - mref);
-    }
-    const R tot = rr::row_allreduce(R{m, s[0] + s[1]}, red, &slot, g.cs, pending);
-    // y = exp(x - M) / S; a row of -inf gives exp(NaN) = NaN, as torch does.
-    const C inv = C(1) / tot.s;
-    VO* yrow = reinterpret_cast<VO*>(y + row * g.y_rs + base);
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) {
-      const VI xv = reinterpret_cast<const VI*>(sx)[v];
-      VO out;
+          for (int e = 0; e < VEC; ++e) acc += rr::c_exp<C>(cvt<C>(xv.v[e]) - ref);
+        }
+        m = cm;
+        sum = acc;
+      },
+      [&] {
+        const R tot = rr::block_allreduce(R{m, sum}, red);
+        M = tot.m;
+        inv = C(1) / tot.s;  // a row of -inf gives exp(NaN) = NaN below, as torch does
+      },
+      [&](const TI* sx, int n, int col0, int64_t row) {
+        VO* yrow = reinterpret_cast<VO*>(y + row * g.y_rs + col0);
+        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
+          const VI xv = reinterpret_cast<const VI*>(sx)[v];
+          VO out;
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) out.v[e] = cvt<TO>(rr::c_exp<C>(cvt<C>(xv.v[e]) - tot.m) * inv);
-      ew::store_cs(yrow + v, out);
-    }
-  });
-  rr::cluster_exit(g.cs, pending);
+          for (int e = 0; e < VEC; ++e) out.v[e] = cvt<TO>(rr::c_exp<C>(cvt<C>(xv.v[e]) - M) * inv);
+          ew::store_cs(yrow + v, out);
+        }
+      });
 }
 
 // Long rows: three strided passes (max, sum, write); passes 2 and 3 re-read from L2.
@@ -103,20 +108,21 @@ __global__ void __launch_bounds__(256) softmax_cols(const TI* __restrict__ x, TO
 
 template <typename TI, typename TO, int VEC>
 int launch_rows_softmax(const TI* x, TO* y, rr::RowGeom g, cudaStream_t st) {
-  int chunk = 0, cs = 1;
-  if (VEC == 1 || !rs::plan_stage(g.cols, (int)sizeof(TI), VEC, &chunk, &cs) ||
-      !rs::stage_aligned(x, g.x_rs, g.rows, (int)sizeof(TI))) {
+  int chunk = 0, nc = 1;
+  if (VEC == 1 || !rs::plan_stream(g.cols, (int)sizeof(TI), VEC, &chunk, &nc) ||
+      !rs::stream_aligned(x, g.x_rs, g.rows, (int)sizeof(TI))) {
     int grid = (int)(g.rows < (int64_t)sm_count() * 8 ? g.rows : (int64_t)sm_count() * 8);
     softmax_rows_looped<TI, TO><<<grid, 512, 0, st>>>(x, y, g);
     NTB_LAUNCH_CHECK();
     return NTB_OK;
   }
-  rs::StageGeom sg{g.rows, g.cols, g.x_rs, g.y_rs, cs, chunk};
+  rs::StreamGeom sg{g.rows, g.cols, g.x_rs, g.y_rs, chunk, nc};
   const int nvec = chunk / VEC;
   int bt = ((nvec + 31) / 32) * 32;
   bt = bt < 32 ? 32 : (bt > 256 ? 256 : bt);
-  const size_t smem = rs::stage_smem_bytes((int64_t)chunk * sizeof(TI));
-  return rs::launch_staged(softmax_staged<TI, TO, VEC>, g.rows, bt, cs, smem, st, x, y, sg, device_error_ptr());
+  const size_t smem = rs::stream_smem_bytes(chunk * (int)sizeof(TI));
+  return rs::launch_stream(softmax_stream<TI, TO, VEC>, g.rows, g.cols * (int64_t)sizeof(TI), nc, bt, smem, st, x,
+                           y, sg, device_error_ptr());
 }
 
 template <typename TI, typename TO>
