@@ -107,9 +107,14 @@ template <typename To>
 struct Cvt<To, __half> {
   __device__ __forceinline__ static To run(__half x) { return static_cast<To>(__half2float(x)); }
 };
+// bfloat16 is the upper half of a float, so widening is a 16-bit shift (exact for every value,
+// NaN payloads included) — one integer instruction.
+__device__ __forceinline__ float bf16_bits_to_float(__nv_bfloat16 x) {
+  return __uint_as_float(static_cast<uint32_t>(__bfloat16_as_ushort(x)) << 16);
+}
 template <typename To>
 struct Cvt<To, __nv_bfloat16> {
-  __device__ __forceinline__ static To run(__nv_bfloat16 x) { return static_cast<To>(__bfloat162float(x)); }
+  __device__ __forceinline__ static To run(__nv_bfloat16 x) { return static_cast<To>(bf16_bits_to_float(x)); }
 };
 // half / bfloat16 destinations
 template <typename From>

@@ -2,9 +2,10 @@
 //
 // Reference algorithm (ntops): kernels/rms_norm.py:10-20 — fp32 sum of squares over the row,
 // rms = sqrt(sum / n + eps), y = x / rms * w; kernels/layer_norm.py:11-31 — fp32 mean, biased
-// variance of (x - mean), y = (x - mean) / sqrt(var + eps) * w + b.  Both read each row once
-// from HBM here (bulk copies stream it through shared memory, see rowstage.cuh) and reduces
-// once; the reference reads it 2 and 3 times.  Statistics are fp32 for half/bf16/fp32 inputs and fp64 for fp64.
+// variance of (x - mean), y = (x - mean) / sqrt(var + eps) * w + b.  Here rows stream through
+// a ring of shared-memory slots filled by bulk copies (rowstage.cuh) and a row that fits the
+// ring or the registers is read from HBM once (the reference reads it 2 and 3 times).
+// Statistics are fp32 for half / bf16 / fp32 inputs and fp64 for fp64.
 #include "rowstage.cuh"
 
 namespace ntb {
@@ -14,56 +15,74 @@ template <typename T> struct Acc { using type = float; };
 template <> struct Acc<double> { using type = double; };
 
 // ------------------------------------------------------------------ RMSNorm ---------------
+// Pass 0 (as chunks arrive): per-thread sum of squares on element pairs; one CTA reduction;
+// pass 1: y = x * rinv * w.  Resident rows are read from HBM once.
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) rms_norm_stream(const T* __restrict__ x, const T* __restrict__ w,
+__global__ void __launch_bounds__(512, 1) rms_norm_ring(const T* __restrict__ x, const T* __restrict__ w,
                                                         T* __restrict__ y, rs::StreamGeom g, double eps,
                                                         unsigned int* err) {
   extern __shared__ __align__(128) uint8_t dyn[];
   using C = typename Acc<T>::type;
-  using R = rr::Sum<C>;
+  using P = typename rs::PairOf<C>::type;
   using V = ew::Vec<T, VEC>;
-  __shared__ R red[32];
-  C ss0, ss1, rinv;
-  rs::stream_rows<T>(
-      x, g, dyn, err, [&] { ss0 = ss1 = C(0); },
-      [&](const T* sx, int n, int) {
-        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
-          const V xv = reinterpret_cast<const V*>(sx)[v];
+  constexpr int NP = VEC / 2;
+  __shared__ rr::Sum<C> red[32];
+  rs::Ring<T> ring(x, g, dyn);
+  ring.start();
+  bool fail = false;
+  const int nc = g.nchunks;
+  for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x) {
+    ring.begin_row();
+    P acc = rs::p_splat(C(0));
+    for (int c = 0; c < nc; ++c) {
+      const V* s = reinterpret_cast<const V*>(ring.wait(fail));
+      const int nv = ring.chunk_len(c) / VEC;
+      for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+        const V xv = s[v];
 #pragma unroll
-          for (int e = 0; e < VEC; e += 2) {
-            const C a = cvt<C>(xv.v[e]);
-            ss0 += a * a;
-            if (e + 1 < VEC) {
-              const C b = cvt<C>(xv.v[e + 1]);
-              ss1 += b * b;
-            }
-          }
+        for (int i = 0; i < NP; ++i) {
+          const P a = rs::pair_at<C>(xv, i);
+          acc = rs::p_fma(a, a, acc);
         }
-      },
-      [&] {
-        const C tot = rr::block_allreduce(R{ss0 + ss1}, red).v;
-        rinv = C(1) / rr::c_sqrt<C>(tot / C(g.cols) + C(eps));
-      },
-      [&](const T* sx, int n, int col0, int64_t row) {
-        V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + col0);
-        const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + col0) : nullptr;
-        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
-          const V xv = reinterpret_cast<const V*>(sx)[v];
-          V out;
-          if (wrow != nullptr) {
-            const V wv = wrow[v];
+      }
+      if (!g.resident) {
+        if ((fail = __syncthreads_or(fail))) break;
+        ring.release(1);
+      }
+    }
+    const C tot = rs::block_reduce_or(rr::Sum<C>{rs::p_hsum(acc)}, red, fail).v;
+    if (fail) break;
+    const P rv = rs::p_splat(C(1) / rr::c_sqrt<C>(tot / C(g.cols) + C(eps)));
+    for (int c = 0; c < nc; ++c) {
+      const V* s = reinterpret_cast<const V*>(g.resident ? ring.chunk(c) : ring.wait(fail));
+      const int nv = ring.chunk_len(c) / VEC;
+      const int64_t col0 = (int64_t)c * g.chunk;
+      V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + col0);
+      const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + col0) : nullptr;
+      for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+        const V xv = s[v];
+        V out;
+        if (wrow != nullptr) {
+          const V wv = wrow[v];
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(cvt<C>(xv.v[e]) * rinv * cvt<C>(wv.v[e]));
-          } else {
+          for (int i = 0; i < NP; ++i)
+            rs::pair_put(out, i, rs::p_mul(rs::p_mul(rs::pair_at<C>(xv, i), rv), rs::pair_at<C>(wv, i)));
+        } else {
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) out.v[e] = cvt<T>(cvt<C>(xv.v[e]) * rinv);
-          }
-          ew::store_cs(yrow + v, out);
+          for (int i = 0; i < NP; ++i) rs::pair_put(out, i, rs::p_mul(rs::pair_at<C>(xv, i), rv));
         }
-      });
+        ew::store_cs(yrow + v, out);
+      }
+      if ((fail = __syncthreads_or(fail))) break;
+      ring.release(1);
+    }
+    if (fail) break;
+  }
+  if (fail && threadIdx.x == 0 && err != nullptr) atomicOr(err, NTB_DEVERR_TIMEOUT);
 }
 
-// Rows too long for the register-resident kernel: strided passes, later ones from L2.
+// Rows that cannot use bulk copies (unaligned, or not vectorisable): strided passes, the later
+// ones from L2.
 template <typename T>
 __global__ void __launch_bounds__(1024) rms_norm_looped(const T* __restrict__ x, const T* __restrict__ w,
                                                         T* __restrict__ y, rr::RowGeom g, double eps) {
@@ -88,74 +107,258 @@ __global__ void __launch_bounds__(1024) rms_norm_looped(const T* __restrict__ x,
   }
 }
 
+// Register-resident RMSNorm (rows of up to 8 chunks): the same arithmetic on the row held in
+// registers (widened to fp32 once); the ring's slots are all look-ahead.
+// FULL: the row fills every vector of every thread (no per-vector predicate).
+template <typename T, int VEC, int NV, int NC, bool FULL>
+__global__ void NTB_REG_BOUNDS(NC) rms_norm_reg(const T* __restrict__ x, const T* __restrict__ w,
+                                                T* __restrict__ y, rs::StreamGeom g, double eps,
+                                                unsigned int* err) {
+  extern __shared__ __align__(128) uint8_t dyn[];
+  using C = float;
+  using P = float2;
+  using V = ew::Vec<T, VEC>;
+  constexpr int NP = VEC / 2;
+  __shared__ rr::Sum<C> red[32];
+  rs::Ring<T> ring(x, g, dyn);
+  rs::RegRow<T, VEC, NV, NC> rr_;
+  rr_.init(g);
+  ring.start();
+  bool fail = false;
+  for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x) {
+    rr_.load(ring, fail);
+    if (fail) break;
+    P a[NC][NV][NP];  // the row widened once to fp32 pairs
+    P acc = rs::p_splat(0.f);
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          a[c][j][i] = rs::pair_at<C>(rr_.v[c][j], i);
+          if (rr_.ok(c, j)) acc = rs::p_fma(a[c][j][i], a[c][j][i], acc);
+        }
+    const C tot = rs::block_reduce_or(rr::Sum<C>{rs::p_hsum(acc)}, red, fail).v;
+    const P rv = rs::p_splat(1.f / sqrtf(tot / (float)g.cols + (float)eps));
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+        if (rr_.ok(c, j)) {
+          const int vi = c * (g.chunk / VEC) + (int)threadIdx.x + j * (int)blockDim.x;  // vector in the row
+          V out;
+          if (w != nullptr) {
+            const V wv = reinterpret_cast<const V*>(w)[vi];
+#pragma unroll
+            for (int i = 0; i < NP; ++i)
+              rs::pair_put(out, i, rs::p_mul(rs::p_mul(a[c][j][i], rv), rs::pair_at<C>(wv, i)));
+          } else {
+#pragma unroll
+            for (int i = 0; i < NP; ++i) rs::pair_put(out, i, rs::p_mul(a[c][j][i], rv));
+          }
+          ew::store_cs(reinterpret_cast<V*>(y + row * g.y_rs) + vi, out);
+        }
+  }
+  if (fail && threadIdx.x == 0 && err != nullptr) atomicOr(err, NTB_DEVERR_TIMEOUT);
+}
+
 // ---------------------------------------------------------------- LayerNorm ---------------
-// One reduction per row: every thread keeps the count, sum and sum of squares of its elements
-// shifted by the first value it saw (shifting keeps the single pass exact enough: the variance
-// of x - K equals that of x and K is within the data's spread), turns them into a
+// Every row is shifted by its first element K (the variance of x - K equals that of x, and K
+// lies within the data, so a mean far from zero neither swamps the sums nor loses the low bits
+// of x - mean).  Resident rows (the whole row stays in shared memory): two-pass statistics from
+// shared memory, each with one CTA reduction — the mean of x - K, then the sum of
+// (x - mean)^2 — and y = (x - mean) * rstd * w + b.  Re-read rows (longer than the ring): every
+// thread keeps the count, sum and sum of squares of its x - K, turns them into a
 // (count, mean, M2) triple, and the triples merge across the CTA with Chan's formula.
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) layer_norm_stream(const T* __restrict__ x, const T* __restrict__ w,
+__global__ void __launch_bounds__(512, 1) layer_norm_ring(const T* __restrict__ x, const T* __restrict__ w,
                                                           const T* __restrict__ b, T* __restrict__ y,
                                                           rs::StreamGeom g, double eps, unsigned int* err) {
   extern __shared__ __align__(128) uint8_t dyn[];
   using C = typename Acc<T>::type;
-  using R = rr::Welford<C>;
+  using P = typename rs::PairOf<C>::type;
   using V = ew::Vec<T, VEC>;
-  __shared__ R red[32];
-  C shift, s, ss, mean, rstd;
-  int cnt;
-  bool have_shift;
-  rs::stream_rows<T>(
-      x, g, dyn, err,
-      [&] {
-        s = ss = C(0);
-        cnt = 0;
-        have_shift = false;
-        shift = C(0);
-      },
-      [&](const T* sx, int n, int) {
-        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
-          const V xv = reinterpret_cast<const V*>(sx)[v];
-          if (!have_shift) {
-            shift = cvt<C>(xv.v[0]);
-            have_shift = true;
+  constexpr int NP = VEC / 2;
+  __shared__ rr::Sum<C> red0[32], red1[32];
+  __shared__ rr::Welford<C> redw[32];
+  rs::Ring<T> ring(x, g, dyn);
+  ring.start();
+  bool fail = false;
+  const int nc = g.nchunks;
+  const C inv_n = C(1) / C(g.cols);
+  for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x) {
+    ring.begin_row();
+    // The mean is carried as shift + mrel: shift is the row's first element and mrel the mean
+    // of x - shift, so x - mean = (x - shift) - mrel keeps its low bits even when the mean is
+    // far from zero relative to the spread (x - shift is exact for such data).
+    C shift = C(0), mrel, rstd;
+    P kv = rs::p_splat(C(0));
+    if (g.resident) {
+      P acc = rs::p_splat(C(0));
+      for (int c = 0; c < nc; ++c) {
+        const V* s = reinterpret_cast<const V*>(ring.wait(fail));
+        if (c == 0) {
+          shift = cvt<C>(reinterpret_cast<const T*>(s)[0]);
+          kv = rs::p_splat(shift);
+        }
+        const int nv = ring.chunk_len(c) / VEC;
+        for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+          const V xv = s[v];
+#pragma unroll
+          for (int i = 0; i < NP; ++i) acc = rs::p_add(acc, rs::p_sub(rs::pair_at<C>(xv, i), kv));
+        }
+      }
+      mrel = rs::block_reduce_or(rr::Sum<C>{rs::p_hsum(acc)}, red0, fail).v * inv_n;
+      if (fail) break;
+      const P mv = rs::p_splat(mrel);
+      P q = rs::p_splat(C(0));
+      for (int c = 0; c < nc; ++c) {
+        const V* s = reinterpret_cast<const V*>(ring.chunk(c));
+        const int nv = ring.chunk_len(c) / VEC;
+        for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+          const V xv = s[v];
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            const P d = rs::p_sub(rs::p_sub(rs::pair_at<C>(xv, i), kv), mv);
+            q = rs::p_fma(d, d, q);
           }
+        }
+      }
+      const C var = rs::block_reduce_or(rr::Sum<C>{rs::p_hsum(q)}, red1, fail).v * inv_n;
+      rstd = C(1) / rr::c_sqrt<C>(var + C(eps));
+    } else {
+      P s1 = rs::p_splat(C(0)), s2 = rs::p_splat(C(0));
+      int cnt = 0;
+      for (int c = 0; c < nc; ++c) {
+        const V* s = reinterpret_cast<const V*>(ring.wait(fail));
+        if (c == 0) {
+          shift = cvt<C>(reinterpret_cast<const T*>(s)[0]);
+          kv = rs::p_splat(shift);
+        }
+        const int nv = ring.chunk_len(c) / VEC;
+        for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+          const V xv = s[v];
           cnt += VEC;
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) {
-            const C d = cvt<C>(xv.v[e]) - shift;
-            s += d;
-            ss += d * d;
+          for (int i = 0; i < NP; ++i) {
+            const P d = rs::p_sub(rs::pair_at<C>(xv, i), kv);
+            s1 = rs::p_add(s1, d);
+            s2 = rs::p_fma(d, d, s2);
           }
         }
-      },
-      [&] {
-        const C nt = C(cnt);
-        const C m_t = cnt ? s / nt : C(0);
-        const C m2_t = cnt ? ss - s * m_t : C(0);
-        const R st = rr::block_allreduce(R{nt, shift + m_t, m2_t > C(0) ? m2_t : C(0)}, red);
-        mean = st.mean;
-        rstd = C(1) / rr::c_sqrt<C>(st.m2 / C(g.cols) + C(eps));
-      },
-      [&](const T* sx, int n, int col0, int64_t row) {
-        V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + col0);
-        const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + col0) : nullptr;
-        const V* brow = b != nullptr ? reinterpret_cast<const V*>(b + col0) : nullptr;
-        for (int v = threadIdx.x; v < n / VEC; v += blockDim.x) {
-          const V xv = reinterpret_cast<const V*>(sx)[v];
-          V wv, bv, out;
-          if (wrow != nullptr) wv = wrow[v];
-          if (brow != nullptr) bv = brow[v];
+        if ((fail = __syncthreads_or(fail))) break;
+        ring.release(1);
+      }
+      // per-thread (count, mean, M2) of x - shift, merged with Chan's formula
+      const C nt = C(cnt), s = rs::p_hsum(s1), ss = rs::p_hsum(s2);
+      const C m_t = cnt ? s / nt : C(0);
+      const C m2_t = cnt ? ss - s * m_t : C(0);
+      const rr::Welford<C> st =
+          rs::block_reduce_or(rr::Welford<C>{nt, m_t, m2_t > C(0) ? m2_t : C(0)}, redw, fail);
+      mrel = st.mean;
+      rstd = C(1) / rr::c_sqrt<C>(st.m2 * inv_n + C(eps));
+    }
+    if (fail) break;
+    const P mv = rs::p_splat(mrel), rv = rs::p_splat(rstd);
+    for (int c = 0; c < nc; ++c) {
+      const V* s = reinterpret_cast<const V*>(g.resident ? ring.chunk(c) : ring.wait(fail));
+      const int nv = ring.chunk_len(c) / VEC;
+      const int64_t col0 = (int64_t)c * g.chunk;
+      V* yrow = reinterpret_cast<V*>(y + row * g.y_rs + col0);
+      const V* wrow = w != nullptr ? reinterpret_cast<const V*>(w + col0) : nullptr;
+      const V* brow = b != nullptr ? reinterpret_cast<const V*>(b + col0) : nullptr;
+      for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+        const V xv = s[v];
+        V wv, bv, out;
+        if (wrow != nullptr) wv = wrow[v];
+        if (brow != nullptr) bv = brow[v];
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) {
-            C r = (cvt<C>(xv.v[e]) - mean) * rstd;  // subtract first: no cancellation
-            if (wrow != nullptr) r *= cvt<C>(wv.v[e]);
-            if (brow != nullptr) r += cvt<C>(bv.v[e]);
-            out.v[e] = cvt<T>(r);
-          }
-          ew::store_cs(yrow + v, out);
+        for (int i = 0; i < NP; ++i) {
+          P r = rs::p_mul(rs::p_sub(rs::p_sub(rs::pair_at<C>(xv, i), kv), mv), rv);  // subtract first
+          if (wrow != nullptr && brow != nullptr) r = rs::p_fma(r, rs::pair_at<C>(wv, i), rs::pair_at<C>(bv, i));
+          else if (wrow != nullptr) r = rs::p_mul(r, rs::pair_at<C>(wv, i));
+          else if (brow != nullptr) r = rs::p_add(r, rs::pair_at<C>(bv, i));
+          rs::pair_put(out, i, r);
         }
-      });
+        ew::store_cs(yrow + v, out);
+      }
+      if ((fail = __syncthreads_or(fail))) break;
+      ring.release(1);
+    }
+    if (fail) break;
+  }
+  if (fail && threadIdx.x == 0 && err != nullptr) atomicOr(err, NTB_DEVERR_TIMEOUT);
+}
+
+// Register-resident LayerNorm: the same three passes (mean of x - K, sum of (x - mean)^2,
+// output) over the row held in registers.
+// FULL as for rms_norm_reg; AFFINE: weight and bias are both given (no null checks).
+template <typename T, int VEC, int NV, int NC, bool FULL, bool AFFINE>
+__global__ void NTB_REG_BOUNDS(NC) layer_norm_reg(const T* __restrict__ x, const T* __restrict__ w,
+                                                  const T* __restrict__ b, T* __restrict__ y,
+                                                  rs::StreamGeom g, double eps, unsigned int* err) {
+  extern __shared__ __align__(128) uint8_t dyn[];
+  using C = float;
+  using P = float2;
+  using V = ew::Vec<T, VEC>;
+  constexpr int NP = VEC / 2;
+  __shared__ rr::Sum<C> red0[32], red1[32];
+  rs::Ring<T> ring(x, g, dyn);
+  rs::RegRow<T, VEC, NV, NC> rr_;
+  rr_.init(g);
+  ring.start();
+  bool fail = false;
+  const C inv_n = 1.f / (float)g.cols;
+  for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x) {
+    const C shift = cvt<C>(rr_.load(ring, fail));
+    if (fail) break;
+    const P kv = rs::p_splat(shift);
+    P d[NC][NV][NP];  // x - K, then x - mean, in fp32 pairs
+    P acc = rs::p_splat(0.f);
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          d[c][j][i] = rs::p_sub(rs::pair_at<C>(rr_.v[c][j], i), kv);
+          if ((FULL || rr_.ok(c, j))) acc = rs::p_add(acc, d[c][j][i]);
+        }
+    const P mv = rs::p_splat(rs::block_reduce_or(rr::Sum<C>{rs::p_hsum(acc)}, red0, fail).v * inv_n);
+    P q = rs::p_splat(0.f);
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          d[c][j][i] = rs::p_sub(d[c][j][i], mv);
+          if ((FULL || rr_.ok(c, j))) q = rs::p_fma(d[c][j][i], d[c][j][i], q);
+        }
+    const C var = rs::block_reduce_or(rr::Sum<C>{rs::p_hsum(q)}, red1, fail).v * inv_n;
+    const P rv = rs::p_splat(1.f / sqrtf(var + (float)eps));
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+        if ((FULL || rr_.ok(c, j))) {
+          const int vi = c * (g.chunk / VEC) + (int)threadIdx.x + j * (int)blockDim.x;  // vector in the row
+          V wv, bv, out;
+          if (AFFINE || w != nullptr) wv = reinterpret_cast<const V*>(w)[vi];
+          if (AFFINE || b != nullptr) bv = reinterpret_cast<const V*>(b)[vi];
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            P r = rs::p_mul(d[c][j][i], rv);
+            if (AFFINE || (w != nullptr && b != nullptr)) r = rs::p_fma(r, rs::pair_at<C>(wv, i), rs::pair_at<C>(bv, i));
+            else if (w != nullptr) r = rs::p_mul(r, rs::pair_at<C>(wv, i));
+            else if (b != nullptr) r = rs::p_add(r, rs::pair_at<C>(bv, i));
+            rs::pair_put(out, i, r);
+          }
+          ew::store_cs(reinterpret_cast<V*>(y + row * g.y_rs) + vi, out);
+        }
+  }
+  if (fail && threadIdx.x == 0 && err != nullptr) atomicOr(err, NTB_DEVERR_TIMEOUT);
 }
 
 template <typename T>
@@ -229,8 +432,8 @@ int launch_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTen
   const T* wp = w ? (const T*)w->data : nullptr;
   const T* bp = b ? (const T*)b->data : nullptr;
   T* yp = (T*)y->data;
-  int chunk = 0, nc = 1;
-  if (VEC == 1 || !rs::plan_stream(g.cols, (int)sizeof(T), VEC, &chunk, &nc) ||
+  rs::RingPlan plan;
+  if (VEC == 1 || !rs::plan_ring(g.rows, g.cols, g.x_rs, g.y_rs, (int)sizeof(T), VEC, &plan) ||
       !rs::stream_aligned(xp, g.x_rs, g.rows, (int)sizeof(T))) {
     int grid = (int)(g.rows < (int64_t)sm_count() * 8 ? g.rows : (int64_t)sm_count() * 8);
     if (layer)
@@ -240,17 +443,38 @@ int launch_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTen
     NTB_LAUNCH_CHECK();
     return NTB_OK;
   }
-  rs::StreamGeom sg{g.rows, g.cols, g.x_rs, g.y_rs, chunk, nc};
-  const int nvec = chunk / VEC;
-  int bt = ((nvec + 31) / 32) * 32;
-  bt = bt < 32 ? 32 : (bt > 256 ? 256 : bt);
-  const size_t smem = rs::stream_smem_bytes(chunk * (int)sizeof(T));
-  const int64_t row_bytes = g.cols * (int64_t)sizeof(T);
   unsigned int* err = device_error_ptr();
-  if (layer)
-    return rs::launch_stream(layer_norm_stream<T, VEC>, g.rows, row_bytes, nc, bt, smem, st, xp, wp, bp, yp, sg,
-                             eps, err);
-  return rs::launch_stream(rms_norm_stream<T, VEC>, g.rows, row_bytes, nc, bt, smem, st, xp, wp, yp, sg, eps, err);
+  if constexpr (VEC >= 2 && !std::is_same_v<T, double>) {
+    rs::RegPlan rp;
+    if (rs::plan_reg(g.rows, g.cols, g.x_rs, g.y_rs, (int)sizeof(T), VEC, &rp)) {
+      const bool full = g.cols == (int64_t)rp.nc_max * rp.threads * rp.nv * VEC && rp.g.chunk == rp.threads * rp.nv * VEC;
+      const auto ring = rs::as_ring_plan(rp);
+      return rs::dispatch_reg<VEC>(rp, [&](auto nv_, auto nc_) {
+        constexpr int NV = decltype(nv_)::value, NC = decltype(nc_)::value;
+        if (layer) {
+          if (full && wp != nullptr && bp != nullptr)
+            return rs::launch_ring(layer_norm_reg<T, VEC, NV, NC, true, true>, ring, (int)sizeof(T), st, xp, wp, bp, yp,
+                                   rp.g, eps, err);
+          if (full)
+            return rs::launch_ring(layer_norm_reg<T, VEC, NV, NC, true, false>, ring, (int)sizeof(T), st, xp, wp, bp,
+                                   yp, rp.g, eps, err);
+          return rs::launch_ring(layer_norm_reg<T, VEC, NV, NC, false, false>, ring, (int)sizeof(T), st, xp, wp, bp, yp,
+                                 rp.g, eps, err);
+        }
+        if (full)
+          return rs::launch_ring(rms_norm_reg<T, VEC, NV, NC, true>, ring, (int)sizeof(T), st, xp, wp, yp, rp.g, eps,
+                                 err);
+        return rs::launch_ring(rms_norm_reg<T, VEC, NV, NC, false>, ring, (int)sizeof(T), st, xp, wp, yp, rp.g, eps,
+                               err);
+      });
+    }
+  }
+  if constexpr (VEC >= 2) {
+    if (layer)
+      return rs::launch_ring(layer_norm_ring<T, VEC>, plan, (int)sizeof(T), st, xp, wp, bp, yp, plan.g, eps, err);
+    return rs::launch_ring(rms_norm_ring<T, VEC>, plan, (int)sizeof(T), st, xp, wp, yp, plan.g, eps, err);
+  }
+  return NTB_OK;
 }
 
 int run_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTensor* b,

@@ -1,9 +1,9 @@
 """Parity of rms_norm, layer_norm, softmax and rotary_position_embedding against the oracle.
 
 Grids follow the reference tests (tests/test_rms_norm.py, test_layer_norm.py:11-37,
-test_softmax.py:11-21, test_rotary_position_embedding.py:48-89) plus bf16, long rows that take
-the thread-block-cluster path (a row split over 2-8 CTAs), rows too long for registers (looped
-path), odd lengths (scalar path) and strided layouts.
+test_softmax.py:11-21, test_rotary_position_embedding.py:48-89) plus bf16, rows that stay
+resident in the shared-memory ring, rows too long for it (re-read path), many rows per CTA (the
+ring wraps), odd lengths (strided fallback), strided layouts and data far from zero.
 """
 
 import random
@@ -72,6 +72,29 @@ def test_long_rows(cols, dtype):
     assert_close(nt.rms_norm(x.to(DEV), cols, w.to(DEV), 1e-6), O.rms_norm(x, cols, w, 1e-6))
     assert_close(nt.layer_norm(x.to(DEV), cols, w.to(DEV), b.to(DEV), 1e-5), O.layer_norm(x, cols, w, b, 1e-5))
     assert_close(nt.softmax(x.to(DEV), -1), O.softmax(x, -1))
+
+
+@pytest.mark.parametrize(
+    "rows,cols,dtype",
+    [(5000, 4096, torch.float32), (1200, 8192, torch.bfloat16), (600, 32768, torch.float32),
+     (300, 65536, torch.float32), (3000, 96, torch.float16), (700, 24576, torch.bfloat16)],
+)
+def test_many_rows(rows, cols, dtype):
+    # more rows than CTAs: each CTA walks several rows and its ring of slots wraps around
+    x = _randn((rows, cols), dtype, 2.0)
+    w = _randn((cols,), dtype)
+    b = _randn((cols,), dtype)
+    xd = x.to(DEV)
+    assert_close(nt.rms_norm(xd, cols, w.to(DEV), 1e-6), O.rms_norm(x, cols, w, 1e-6))
+    assert_close(nt.layer_norm(xd, cols, w.to(DEV), b.to(DEV), 1e-5), O.layer_norm(x, cols, w, b, 1e-5))
+    assert_close(nt.softmax(xd, -1), O.softmax(x, -1))
+
+
+@pytest.mark.parametrize("cols", [4096, 65536])
+def test_layer_norm_offset_data(cols):
+    # mean far from zero relative to the spread: the statistics must not cancel
+    x = torch.randn(64, cols) * 0.01 + 1000.0
+    assert_close(nt.layer_norm(x.to(DEV), cols, None, None, 1e-5), O.layer_norm(x, cols, None, None, 1e-5))
 
 
 def test_strided_rows():
