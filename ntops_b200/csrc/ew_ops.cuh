@@ -92,16 +92,15 @@ struct BitwiseNot {
   template <typename T> __device__ T operator()(T x) const { return T(~x); }
   __device__ bool operator()(bool x) const { return !x; }
 };
-// clamp with scalar bounds: NaN propagates; min applied before max (torch.clamp).
+// clamp with scalar bounds: NaN propagates; min applied before max (torch.clamp).  Branch-free:
+// both compares are false for NaN, and an absent bound is replaced on the host side of the
+// functor by the type's extreme (-inf / +inf for floats), which never wins a compare.
 template <typename M>
 struct ClampScalar {
   M lo, hi;
-  int has_lo, has_hi;
   __device__ M operator()(M x) const {
-    if (is_nan(x)) return x;
-    if (has_lo) x = x < lo ? lo : x;
-    if (has_hi) x = x > hi ? hi : x;
-    return x;
+    x = x < lo ? lo : x;
+    return x > hi ? hi : x;
   }
 };
 
@@ -160,16 +159,26 @@ struct TanhFast { __device__ float operator()(float x) const { return hw_tanh(x)
 struct RsqrtFast { __device__ float operator()(float x) const { return hw_rsqrt(x); } };
 // x^e = 2^(e * log2|x|) with the sign of an odd integer exponent; NaN for a negative base with a
 // fractional exponent; pow(x, 0) = pow(1, e) = 1 (C / torch semantics).
+// C / torch pow sign and domain rules applied to r = |a|^b, as selects (no divergent
+// branches): a base with the sign bit set (negative, -0, -inf) and an odd integer exponent
+// flips the sign; a finite negative base with a non-integer exponent gives NaN; pow(-1, +-inf),
+// pow(x, 0) and pow(1, y) are 1.  Exponents of magnitude >= 2^24 are even integers.
+__device__ __forceinline__ float pow_rules(float a, float b, float r) {
+  const bool neg = __float_as_int(a) < 0;
+  const bool nonint = b != truncf(b);
+  const bool small = fabsf(b) < 16777216.f;
+  const bool odd = small && (((int)b) & 1);
+  const float rn = nonint ? ((a < 0.f && a > -INFINITY) ? __int_as_float(0x7fffffff) : r)
+                          : (small ? (odd ? -r : r) : (a == -1.f ? 1.f : r));
+  r = neg ? rn : r;
+  return (b == 0.f || a == 1.f) ? 1.f : r;
+}
+
+// 16-bit outputs: 2^(b log2|a|) with the hardware approximations (relative error ~|b log2 a|
+// * 2^-22, far inside the outputs' rounding); subnormal fp32 values (reachable only from
+// bf16 bases or results below 2^-126) flush to zero.
 struct PowFast {
-  __device__ float operator()(float a, float b) const {
-    if (b == 0.f || a == 1.f) return 1.f;
-    float r = hw_ex2(b * hw_lg2(fabsf(a)));
-    if (a < 0.f) {
-      if (b != truncf(b)) return __int_as_float(0x7fffffff);
-      if (fabsf(b) < 16777216.f && (((int)b) & 1)) r = -r;
-    }
-    return r;
-  }
+  __device__ float operator()(float a, float b) const { return pow_rules(a, b, hw_ex2(b * hw_lg2(fabsf(a)))); }
 };
 
 // ----------------------------------------------------------------------- binary -----------
@@ -230,7 +239,15 @@ struct DivFloor {
   }
 };
 struct Pow {
-  __device__ float operator()(float a, float b) const { return m_pow(a, b); }
+  // fp32: 2^(b * log2|a|) with the hardware approximations when |b| <= 8 and |b log2|a|| <= 8
+  // (results in [2^-8, 2^8]): the base-2 log is within 2^-22 absolute (or relative, whichever
+  // is larger), so the exponent is off by at most 8 * 2^-22 and the result by ~1.6e-6
+  // relative; powf otherwise (large exponents, zeros, subnormals, infinities, NaN).
+  __device__ float operator()(float a, float b) const {
+    const float t = b * hw_lg2(fabsf(a));
+    if (fabsf(t) <= 8.f && fabsf(b) <= 8.f) return pow_rules(a, b, hw_ex2(t));
+    return m_pow(a, b);
+  }
   __device__ double operator()(double a, double b) const { return m_pow(a, b); }
   // Integer power by squaring; negative exponents give 0 except for bases 1 and -1.
   template <typename T> __device__ T operator()(T base, T e) const {

@@ -1,6 +1,8 @@
 // ntb_unary: the one-input elementwise operators (neg, abs, relu, exp, sigmoid, silu, gelu,
 // tanh, rsqrt, sin, cos, isnan, isinf, bitwise_not, clamp with scalar bounds).
 // Launch plumbing is in elementwise.cuh; per-element math in ew_ops.cuh.
+#include <limits>
+
 #include "elementwise.cuh"
 #include "ew_ops.cuh"
 
@@ -63,16 +65,18 @@ int run_clamp(const NtbTensor* x, const NtbTensor* y, const double* sc, int nsc,
   NTB_ARG(sc != nullptr && nsc >= 4, "clamp needs 4 scalars (min, max, has_min, has_max)");
   NTB_UNSUP(x->dtype == y->dtype, "clamp: output dtype must equal input dtype");
   const NtbTensor* xs[1] = {x};
-  const int has_lo = sc[2] != 0.0, has_hi = sc[3] != 0.0;
+  const bool has_lo = sc[2] != 0.0, has_hi = sc[3] != 0.0;
   if (dtype_is_float(x->dtype)) {
     NTB_DISPATCH_FLOAT(x->dtype, {
       using M = typename OpMath<scalar_t>::type;
-      ops::ClampScalar<M> op{(M)sc[0], (M)sc[1], has_lo, has_hi};
+      ops::ClampScalar<M> op{has_lo ? (M)sc[0] : -std::numeric_limits<M>::infinity(),
+                             has_hi ? (M)sc[1] : std::numeric_limits<M>::infinity()};
       return ew::launch<1, scalar_t, scalar_t>(op, xs, y, st);
     });
   }
   NTB_DISPATCH_INT(x->dtype, {
-    ops::ClampScalar<scalar_t> op{(scalar_t)sc[0], (scalar_t)sc[1], has_lo, has_hi};
+    ops::ClampScalar<scalar_t> op{has_lo ? (scalar_t)sc[0] : std::numeric_limits<scalar_t>::lowest(),
+                                  has_hi ? (scalar_t)sc[1] : std::numeric_limits<scalar_t>::max()};
     return ew::launch<1, scalar_t, scalar_t>(op, xs, y, st);
   });
   return NTB_OK;

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import oracle.ops as O
-from tests.utils import assert_close, case_id, float_cases, int_cases, randint_full
+from tests.utils import TOL, assert_close, case_id, float_cases, int_cases, randint_full
 
 pytestmark = pytest.mark.gpu
 
@@ -100,6 +100,44 @@ def test_pow(case):
     a = (torch.rand(shape) * 8 - 4).to(dtype)
     e = (torch.rand(shape) * 1.5 + 0.5).to(dtype)
     assert_close(nt.pow(a.to(DEV), e.to(DEV)), O.pow(a, e), equal_nan=True)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16, torch.float64])
+def test_pow_special_values(dtype):
+    # every pairing of signed zeros, infinities, NaN, +-1, integer / odd / fractional exponents
+    vals = [float("-inf"), -3.0, -2.0, -1.0, -0.5, -0.0, 0.0, 0.5, 1.0, 2.0, 3.0, float("inf"), float("nan")]
+    a = torch.tensor(vals, dtype=dtype).repeat_interleave(len(vals))
+    e = torch.tensor(vals, dtype=dtype).repeat(len(vals))
+    got = nt.pow(a.to(DEV), e.to(DEV)).cpu()
+    want = torch.pow(a.double(), e.double()).to(dtype)
+    torch.testing.assert_close(got, want, equal_nan=True, rtol=TOL[dtype][0], atol=TOL[dtype][1])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_pow_wide_range(dtype):
+    # bases over many octaves and exponents beyond the fast path's |b|, |b log2 a| <= 8 window
+    g = torch.Generator().manual_seed(7)
+    a = torch.exp2(torch.rand(20000, generator=g) * 40 - 20) * torch.where(torch.rand(20000, generator=g) < 0.3, -1.0, 1.0)
+    e = torch.rand(20000, generator=g) * 24 - 12
+    e[::4] = torch.round(e[::4])  # integer exponents, with negative bases
+    a, e = a.to(dtype), e.to(dtype)
+    got = nt.pow(a.to(DEV), e.to(DEV)).cpu()
+    want = torch.pow(a.double(), e.double())
+    finite = torch.isfinite(want) & (want.abs() < torch.finfo(dtype).max) & (want.abs() > torch.finfo(dtype).tiny)
+    torch.testing.assert_close(got[finite].double(), want[finite], rtol=TOL[dtype][0], atol=0)
+    assert torch.equal(torch.isnan(got), torch.isnan(want.to(dtype)))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16, torch.int32])
+def test_clamp_scalar_edges(dtype):
+    if dtype.is_floating_point:
+        x = torch.tensor([float("nan"), float("-inf"), float("inf"), -2.0, -1.0, 0.0, 1.0, 2.0], dtype=dtype)
+    else:
+        x = torch.tensor([-2**31, -5, -1, 0, 1, 5, 2**31 - 1], dtype=dtype)
+    for lo, hi in ((-1, 1), (None, 1), (-1, None), (2, 1)):
+        got = nt.clamp(x.to(DEV), lo, hi).cpu()
+        want = torch.clamp(x, lo, hi)
+        torch.testing.assert_close(got, want, equal_nan=True, rtol=0, atol=0)
 
 
 @pytest.mark.parametrize("op", ["eq", "ne", "lt", "le", "gt", "ge"])
