@@ -45,8 +45,9 @@ GLOBAL_BATCH = 16
 SEQ = 2048
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) of one launch of the fused gate/up (SwiGLU) projection at the full
-# chain size, from the ncu capture summarised in profiles/ (None until captured).
-SWIGLU_GEMM_TRAFFIC = None
+# chain size: ncu dram__bytes_read.sum 2.344712 GB + dram__bytes_write.sum 0.931517 GB
+# (profiles/gemm_tc_kernel-swiglu_32768x28672x4096_bf16.md).
+SWIGLU_GEMM_TRAFFIC = 3_276_228_928
 
 
 def load_peaks():
