@@ -12,8 +12,10 @@
 // merges the chunks: O = sum_c O_c e^(m_c - M) / sum_c l_c e^(m_c - M).  Both are HBM-bound
 // on the K / V bytes.
 #include <mutex>
+#include <type_traits>
 
 #include "elementwise.cuh"
+#include "sm100.cuh"
 
 namespace ntb {
 namespace decode {
@@ -32,7 +34,27 @@ struct Args {
   int vec;  // K / V rows load as 16-byte vectors
   float scale;
   float* ws;  // [B, Hq, Sq, splits, Dv + 2]: unnormalised O, then max, sum
+  unsigned int* err;  // device error word (bounded waits of decode_stream)
 };
+
+// Bulk global -> shared copy (both addresses 16-byte aligned, bytes a multiple of 16) completing
+// on `bar`; no multicast.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          sm100::smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(sm100::smem_u32(bar))
+      : "memory");
+}
+
+// Two packed 16-bit values (element 0 in the low half) widened to fp32.
+template <typename T> __device__ __forceinline__ float2 widen2(uint32_t w);
+template <> __device__ __forceinline__ float2 widen2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <> __device__ __forceinline__ float2 widen2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
 
 __host__ __device__ inline int64_t ws_floats(const Args& a) {
   return (int64_t)a.B * a.Hq * a.Sq * a.splits * (a.Dv + 2);
@@ -162,6 +184,227 @@ __global__ void __launch_bounds__(kThreads) decode_partial(Args a) {
   }
 }
 
+// Streaming split-KV kernel for 16-bit K / V with head_dim 64 or 128, at most 8 query rows per
+// kv head and no additive mask (the common decode case).  Warp 4 is a producer: its lane 0
+// streams the CTA's key chunk in blocks of 32 keys through a ring of kStages shared-memory
+// stages with bulk copies (one copy per block of K and of V when a head's rows are contiguous,
+// one per key row otherwise), so ~kStages x 16 KB per CTA are in flight whatever the register
+// budget.  Warps 0-3 consume: each takes 8 keys of every block; a key row is read by D / 8 lanes
+// (16 bytes each, conflict-free), every lane keeps its 8 dimensions of the R query rows
+// (pre-scaled into base-2 units), the running max / sum and its 8 output columns per row in
+// registers; a key's R dot products are finished with a butterfly over its D / 8 lanes and the
+// online-softmax max is shared across the warp so all lanes use one reference.  The 4 consumer
+// warps merge through shared memory into one partial per row (same workspace format as
+// decode_partial: O unnormalised, max in natural-log units, sum).
+constexpr int kStreamKeys = 32;   // keys per stage
+constexpr int kStages = 4;
+constexpr int kStreamThreads = 160;
+
+template <int D>
+struct StreamSmem {
+  static constexpr int BLOCK = kStreamKeys * D * 2;  // bytes of one K (or V) block, 16-bit
+  static constexpr int STAGE = 2 * BLOCK;
+  static constexpr int BAR_OFF = kStages * STAGE;
+  static constexpr int TOTAL = BAR_OFF + 2 * kStages * 8 + 16;
+};
+
+template <typename T, int D, int R>
+__global__ void __launch_bounds__(kStreamThreads) decode_stream(Args a) {
+  constexpr int LPK = D / 8;          // lanes per key row (one 16-byte vector each)
+  constexpr int KPW = 32 / LPK;       // key rows per warp step
+  constexpr int U = 8 / KPW;          // steps per block (8 keys of each block per warp)
+  using SM = StreamSmem<D>;
+  extern __shared__ __align__(128) uint8_t dyn[];
+  __shared__ float sm_m[4][R], sm_l[4][R];
+  __shared__ __align__(16) float sm_acc[4][R][D];
+  uint64_t* full = reinterpret_cast<uint64_t*>(dyn + SM::BAR_OFF);
+  uint64_t* empty = full + kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+  const int split = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = a.group * a.Sq;
+  const int k_begin = split * a.chunk;
+  const int k_end = min(a.Skv, k_begin + a.chunk);
+  const int nblk = k_end > k_begin ? (k_end - k_begin + kStreamKeys - 1) / kStreamKeys : 0;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kStages; ++st) {
+      sm100::mbar_init(&full[st], 1);
+      sm100::mbar_init(&empty[st], 4);
+    }
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------- producer ----
+    if (lane == 0) {
+      const T* Kh = reinterpret_cast<const T*>(a.k) + (int64_t)b * a.k_b + (int64_t)hkv * a.k_h;
+      const T* Vh = reinterpret_cast<const T*>(a.v) + (int64_t)b * a.v_b + (int64_t)hkv * a.v_h;
+      int issued = 0;
+      for (int i = 0; i < nblk; ++i) {
+        const int st = i % kStages;
+        if (i >= kStages && !sm100::mbar_wait(&empty[st], (uint32_t)(((i / kStages) - 1) & 1), abort_flag, a.err))
+          break;
+        const int key0 = k_begin + i * kStreamKeys;
+        const int nk = min(kStreamKeys, k_end - key0);
+        const uint32_t row_bytes = D * 2;
+        sm100::mbar_arrive_expect_tx(&full[st], 2u * nk * row_bytes);
+        uint8_t* sk = dyn + st * SM::STAGE;
+        uint8_t* sv = sk + SM::BLOCK;
+        if (a.k_s == D) {
+          bulk_g2s(sk, Kh + (int64_t)key0 * D, nk * row_bytes, &full[st]);
+        } else {
+          for (int r = 0; r < nk; ++r) bulk_g2s(sk + r * row_bytes, Kh + (int64_t)(key0 + r) * a.k_s, row_bytes, &full[st]);
+        }
+        if (a.v_s == D) {
+          bulk_g2s(sv, Vh + (int64_t)key0 * D, nk * row_bytes, &full[st]);
+        } else {
+          for (int r = 0; r < nk; ++r) bulk_g2s(sv + r * row_bytes, Vh + (int64_t)(key0 + r) * a.v_s, row_bytes, &full[st]);
+        }
+        ++issued;
+      }
+      // Leave no copy in flight: wait (bounded) for the last phase of every stage used.
+      for (int i = issued - kStages > 0 ? issued - kStages : 0; i < issued; ++i)
+        sm100::mbar_wait_unwind(&full[i % kStages], (uint32_t)((i / kStages) & 1));
+    }
+  } else {
+    // ------------------------------------------------------------------ consumers ----
+    const int sub = lane % LPK, slot = lane / LPK;
+    const float qs = a.scale * 1.4426950408889634f;  // scores in base-2 units
+    const int off = a.causal == 2 ? a.Skv - a.Sq : 0;
+    float2 q2[R][4];
+    int kmax[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      kmax[r] = -1;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q2[r][i] = make_float2(0.f, 0.f);
+      if (r < rows) {
+        const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
+        const T* qr = reinterpret_cast<const T*>(a.q) + (int64_t)b * a.q_b + (int64_t)hq * a.q_h + (int64_t)s * a.q_s + sub * 8;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q2[r][i] = make_float2(cvt<float>(qr[2 * i]) * qs, cvt<float>(qr[2 * i + 1]) * qs);
+        kmax[r] = a.causal ? min(a.Skv - 1, s + off) : a.Skv - 1;
+      }
+    }
+    float m[R], l[R];
+    float2 acc[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      m[r] = -INFINITY;
+      l[r] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[r][i] = make_float2(0.f, 0.f);
+    }
+    for (int i = 0; i < nblk; ++i) {
+      const int st = i % kStages;
+      if (!sm100::mbar_wait(&full[st], (uint32_t)((i / kStages) & 1), abort_flag, a.err)) break;
+      const uint8_t* sk = dyn + st * SM::STAGE;
+      const uint8_t* sv = sk + SM::BLOCK;
+      const int key0 = k_begin + i * kStreamKeys;
+      float sc[U][R];
+      uint4 vv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int kk = warp * 8 + u * KPW + slot;  // key within the block
+        const int key = key0 + kk;
+        const bool valid = key < k_end;
+        const uint4 kv = *reinterpret_cast<const uint4*>(sk + kk * D * 2 + sub * 16);
+        const uint4 vl = *reinterpret_cast<const uint4*>(sv + kk * D * 2 + sub * 16);
+        vv[u] = valid ? vl : make_uint4(0, 0, 0, 0);  // rows past the chunk hold stale bytes
+        const uint32_t w4[4] = {kv.x, kv.y, kv.z, kv.w};
+        float2 kf[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) kf[e] = widen2<T>(w4[e]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float2 d2 = __fmul2_rn(q2[r][0], kf[0]);
+#pragma unroll
+          for (int e = 1; e < 4; ++e) d2 = __ffma2_rn(q2[r][e], kf[e], d2);
+          float dot = d2.x + d2.y;
+#pragma unroll
+          for (int o = LPK / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+          sc[u][r] = (valid && key <= kmax[r]) ? dot : -INFINITY;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&empty[st]);  // this warp is done reading the stage
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float mb = sc[0][r];
+#pragma unroll
+        for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u][r]);
+#pragma unroll
+        for (int o = LPK; o < 32; o <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const float m_new = fmaxf(m[r], mb);
+        const float m_ref = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = sm100::ex2_approx(m[r] - m_ref);
+        m[r] = m_new;
+        float ps = 0.f;
+        float2 pv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pv[e] = __fmul2_rn(acc[r][e], make_float2(alpha, alpha));
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const float pu = sm100::ex2_approx(sc[u][r] - m_ref);
+          ps += pu;
+          const uint32_t w4[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) pv[e] = __ffma2_rn(make_float2(pu, pu), widen2<T>(w4[e]), pv[e]);
+        }
+        l[r] = l[r] * alpha + ps;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[r][e] = pv[e];
+      }
+    }
+    // Sum the key slots of the warp (every slot shares the warp's reference max).
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+#pragma unroll
+      for (int o = LPK; o < 32; o <<= 1) {
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[r][e].x += __shfl_xor_sync(0xffffffffu, acc[r][e].x, o);
+          acc[r][e].y += __shfl_xor_sync(0xffffffffu, acc[r][e].y, o);
+        }
+      }
+      if (slot == 0) {
+        if (sub == 0) {
+          sm_m[warp][r] = m[r];
+          sm_l[warp][r] = l[r];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) *reinterpret_cast<float2*>(&sm_acc[warp][r][sub * 8 + 2 * e]) = acc[r][e];
+      }
+    }
+  }
+  __syncthreads();
+  if (*abort_flag) return;  // the device error word is already set
+  for (int idx = threadIdx.x; idx < R * (D + 2); idx += kStreamThreads) {
+    const int r = idx / (D + 2), d = idx % (D + 2);
+    if (r >= rows) continue;
+    float M = sm_m[0][r];
+#pragma unroll
+    for (int w = 1; w < 4; ++w) M = fmaxf(M, sm_m[w][r]);
+    const float Mref = M == -INFINITY ? 0.f : M;
+    float val;
+    if (d == D) {
+      val = M == -INFINITY ? -INFINITY : M * 0.6931471805599453f;  // base 2 -> natural-log units
+    } else {
+      val = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float f = sm100::ex2_approx(sm_m[w][r] - Mref);
+        val += (d < D ? sm_acc[w][r][d] : sm_l[w][r]) * f;
+      }
+    }
+    const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
+    a.ws[((((int64_t)b * a.Hq + hq) * a.Sq + s) * a.splits + split) * (D + 2) + d] = val;
+  }
+}
+
 // One CTA per (batch, q head, query row): merges the chunks' partial results.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) decode_merge(Args a) {
@@ -232,10 +475,10 @@ int plan(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTe
             "attn_mask must be expanded to [B, Hq, Sq, Skv]");
     NTB_UNSUP(mask->dtype == q->dtype, "attn_mask dtype must equal the query dtype");
   }
-  // Split the key range so that (batch x kv heads x chunks) fills the GPU four times over, with
-  // chunks of at least 256 keys.
+  // Split the key range so that (batch x kv heads x chunks) gives about six CTAs per SM (two
+  // waves of the streaming kernel's three resident CTAs), with chunks of at least 256 keys.
   const int64_t units = (int64_t)a->B * a->Hkv;
-  int splits = (int)((4 * sm_count() + units - 1) / units);
+  int splits = (int)((6 * sm_count() + units - 1) / units);
   const int max_splits = (a->Skv + 255) / 256;
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
@@ -262,6 +505,7 @@ int plan(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTe
     a->m_b = a->m_h = a->m_q = a->m_k = 0;
   }
   a->ws = nullptr;
+  a->err = device_error_ptr();
   {
     const int es = dtype_size(q->dtype), ve = 16 / es;
     a->vec = a->D % ve == 0 && a->Dv % ve == 0 && a->k_s % ve == 0 && a->v_s % ve == 0 &&
@@ -290,8 +534,43 @@ int launch_dc(const Args& a, size_t smem, cudaStream_t st) {
   return launch_partial<T, RPW, 8>(a, smem, st);
 }
 
+// The streaming kernel serves 16-bit K / V rows readable as 16-byte vectors, head_dim 64 or 128
+// for both K and V, at most 8 query rows per kv head and no additive mask.
+template <typename T, int D, int R>
+int launch_stream_r(const Args& a, cudaStream_t st) {
+  auto k = decode_stream<T, D, R>;
+  const size_t smem = StreamSmem<D>::TOTAL;
+  if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k<<<dim3(a.splits, a.Hkv, a.B), kStreamThreads, smem, st>>>(a);
+  NTB_LAUNCH_CHECK();
+  return NTB_OK;
+}
+
+// The streaming kernel serves 16-bit K / V rows readable as 16-byte vectors, head_dim 64 or 128
+// for both K and V, at most 8 query rows per kv head and no additive mask.
+template <typename T, int D>
+int launch_stream_d(const Args& a, cudaStream_t st) {
+  const int rows = a.group * a.Sq;
+  if (rows <= 1) return launch_stream_r<T, D, 1>(a, st);
+  if (rows <= 2) return launch_stream_r<T, D, 2>(a, st);
+  if (rows <= 4) return launch_stream_r<T, D, 4>(a, st);
+  return launch_stream_r<T, D, 8>(a, st);
+}
+
 template <typename T>
 int launch_typed(const Args& a, cudaStream_t st) {
+  if constexpr (!std::is_same_v<T, float>) {
+    if (a.mask == nullptr && a.vec && a.D == a.Dv && (a.D == 64 || a.D == 128) && a.group * a.Sq <= 8 &&
+        a.chunk % 32 == 0 && a.Hkv <= 65535 && a.B <= 65535) {
+      const int rc = a.D == 128 ? launch_stream_d<T, 128>(a, st) : launch_stream_d<T, 64>(a, st);
+      if (rc != NTB_OK) return rc;
+      const int64_t rows = (int64_t)a.B * a.Hq * a.Sq;
+      NTB_UNSUP(rows <= 0x7fffffffLL, "too many rows");
+      decode_merge<T><<<(unsigned)rows, kThreads, 0, st>>>(a);
+      NTB_LAUNCH_CHECK();
+      return NTB_OK;
+    }
+  }
   const size_t smem = sizeof(float) * ((size_t)a.group * a.Sq * a.D + (size_t)kKeys * (a.D + 1) +
                                        (size_t)kKeys * (a.Dv + 1) + 4 * kKeys);
   NTB_UNSUP(a.Hkv <= 65535 && a.B <= 65535, "too many heads / batches");
