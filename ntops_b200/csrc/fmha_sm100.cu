@@ -280,29 +280,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::tc_fence_after();
       const int k0 = j * BLK;
       const bool need_mask = (k0 + BLK - 1 > kmax);
-      // pass 1: row max (8 independent chains)
+      // The row's 128 scores: four TMEM loads in flight, one wait.
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, sr[c]);
+      sm100::tmem_ld_wait();
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (k0 + c * 32 + i > kmax) sr[c][i] = __float_as_uint(-INFINITY);
+      }
+      // row max (8 independent chains)
       float mx8[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) mx8[c] = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, r);
-        sm100::tmem_ld_wait();
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(r[i]);
-          if (need_mask && k0 + c * 32 + i > kmax) v = -INFINITY;
-          mx8[i & 7] = fmaxf(mx8[i & 7], v);
-        }
-      }
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[c][i]));
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_blk = mx * p.scale_log2;
-      // Rescale O and l only when the max grows by more than the threshold.
+      // Rescale O and l only when the max grows by more than the threshold (done after P is
+      // written, before P is published: PV_t(j) must accumulate into the rescaled O).
       const bool grow = m_blk > m_used + kRescaleThreshold;
+      const float m_prev = m_used;
+      if (grow) m_used = m_blk;
+      const float m_ref = m_used == -INFINITY ? 0.f : m_used;
+      // P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = sm100::ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), p.scale_log2, -m_ref));
+          const float p1 = sm100::ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), p.scale_log2, -m_ref));
+          sum4[i & 3] += p0 + p1;
+          pk[i] = pack2<T>(p0, p1);
+        }
+        sm100::tmem_st_32x32b_x16(s_tmem + c * 16, pk);
+      }
       if (__any_sync(0xffffffffu, grow && j > 0)) {
-        const float alpha = grow ? exp2f(m_used - m_blk) : 1.f;
+        const float alpha = grow ? exp2f(m_prev - m_blk) : 1.f;
         // PV_t(j-1) (and, by commit order, every earlier PV of this tile) must be complete.
         if (!sm100::mbar_wait(&pv_done[t], (uint32_t)((j - 1) & 1), abort_flag, p.err)) { ok = false; break; }
         sm100::tc_fence_after();
@@ -315,32 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
           sm100::tmem_st_32x32b_x32(o_tmem + c * 32, r);
         }
-        sm100::tmem_st_wait();
         l *= alpha;
-      }
-      if (grow) m_used = m_blk;
-      const float m_ref = m_used == -INFINITY ? 0.f : m_used;
-      // pass 2: P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, r);
-        sm100::tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float s0 = __uint_as_float(r[2 * i]), s1 = __uint_as_float(r[2 * i + 1]);
-          if (need_mask) {
-            if (k0 + c * 32 + 2 * i > kmax) s0 = -INFINITY;
-            if (k0 + c * 32 + 2 * i + 1 > kmax) s1 = -INFINITY;
-          }
-          const float p0 = sm100::ex2_approx(fmaf(s0, p.scale_log2, -m_ref));
-          const float p1 = sm100::ex2_approx(fmaf(s1, p.scale_log2, -m_ref));
-          sum4[i & 3] += p0 + p1;
-          pk[i] = pack2<T>(p0, p1);
-        }
-        sm100::tmem_st_32x32b_x16(s_tmem + c * 16, pk);
       }
       l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       sm100::tmem_st_wait();
