@@ -88,6 +88,13 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Three-input maximum (sm_100 max.f32 with three sources; a NaN source is ignored like fmaxf).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // TMEM columns: S_t at 128 t (P_t written over its first 64 columns), O_t at 256 + 128 t.
 constexpr uint32_t kSCol = 0;
 constexpr uint32_t kOCol = 256;
@@ -292,16 +299,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (k0 + c * 32 + i > kmax) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      // row max (8 independent chains)
-      float mx8[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) mx8[c] = -INFINITY;
+      // row max: three-input max over pairs, 4 independent chains
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[c][i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int i = 0; i < 16; ++i)
+          mx4[i & 3] = max3f(mx4[i & 3], __uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1]));
+      const float mx = max3f(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
       const float m_blk = mx * p.scale_log2;
       // Rescale O and l only when the max grows by more than the threshold (done after P is
       // written, before P is published: PV_t(j) must accumulate into the rescaled O).
@@ -309,20 +314,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_prev = m_used;
       if (grow) m_used = m_blk;
       const float m_ref = m_used == -INFINITY ? 0.f : m_used;
-      // P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      // P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns; the
+      // argument and the row sum use the packed fp32x2 instructions
+      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_ref, -m_ref);
+      float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = sm100::ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), p.scale_log2, -m_ref));
-          const float p1 = sm100::ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), p.scale_log2, -m_ref));
-          sum4[i & 3] += p0 + p1;
-          pk[i] = pack2<T>(p0, p1);
+          float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])), sc2, nm2);
+          x.x = sm100::ex2_approx(x.x);
+          x.y = sm100::ex2_approx(x.y);
+          sum2[i & 1] = __fadd2_rn(sum2[i & 1], x);
+          pk[i] = pack2<T>(x.x, x.y);
         }
         sm100::tmem_st_32x32b_x16(s_tmem + c * 16, pk);
       }
+      const float2 sum = __fadd2_rn(sum2[0], sum2[1]);
       if (__any_sync(0xffffffffu, grow && j > 0)) {
         const float alpha = grow ? exp2f(m_prev - m_blk) : 1.f;
         // PV_t(j-1) (and, by commit order, every earlier PV of this tile) must be complete.
@@ -339,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         l *= alpha;
       }
-      l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      l += sum.x + sum.y;
       sm100::tmem_st_wait();
       sm100::tc_fence_before();
       sm100::mbar_arrive(&p_full[t]);
