@@ -35,7 +35,15 @@ namespace fmha {
 
 constexpr int BLK = 128;         // query rows per Q tile and keys per KV block
 constexpr int kTiles = 2;        // Q tiles per CTA (ping-pong between two softmax warpgroups)
-constexpr int kThreads = 320;    // warps 0-3 softmax tile 0, 4-7 softmax tile 1, 8 TMA, 9 MMA
+constexpr int kThreads = 384;    // warps 0-3 softmax tile 0, 4-7 softmax tile 1, 8 TMA, 9 MMA, 10-11 idle
+// Register split (setmaxnreg): the launch gives every thread kLaunchRegs; the TMA / MMA
+// warpgroup (warps 8-11) drops to kProdRegs and the two softmax warpgroups rise to kSoftRegs.
+// 8 * 32 * kSoftRegs + 4 * 32 * kProdRegs must not exceed kThreads * kLaunchRegs, or the raise
+// would wait forever; the host checks the compiled register count before launching.
+constexpr int kLaunchRegs = 168;
+constexpr int kProdRegs = 96;
+constexpr int kSoftRegs = 200;
+static_assert(8 * 32 * kSoftRegs + 4 * 32 * kProdRegs <= kThreads * kLaunchRegs, "register split too large");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;
 
@@ -163,6 +171,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= 8) {
+    // TMA / MMA warpgroup: few registers (all four warps execute the split together)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs));
   if (warp == 8) {
     // ------------------------------------------------------------------ TMA producer ----
     if (lane == 0 && nkv > 0) {
@@ -268,8 +279,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::mbar_wait_unwind(done_bar, 0);
     }
     __syncwarp();
+  }
   } else {
     // ------------------------------------------------------- softmax warpgroups ----
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftRegs));
     const int t = warp >> 2;                       // Q tile of this warpgroup
     const int wq = warp & 3;                       // TMEM lane quarter
     const int row = q0 + t * BLK + wq * 32 + lane; // query row of this thread
@@ -514,6 +527,16 @@ int launch_tc(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, Params
       NTB_OK)
     return rc;
   auto kernel = fmha_tc_kernel<T, D>;
+  {
+    // The register split assumes the compiled launch register count (kLaunchRegs).
+    static std::atomic<int> regs_ok{0};
+    if (regs_ok.load() == 0) {
+      cudaFuncAttributes fa;
+      NTB_CUDA(cudaFuncGetAttributes(&fa, kernel));
+      regs_ok.store(fa.numRegs >= kLaunchRegs ? 1 : -1);
+    }
+    NTB_UNSUP(regs_ok.load() == 1, "attention kernel built with fewer than %d registers per thread", kLaunchRegs);
+  }
   static std::atomic<uint64_t> attr_set{0};
   const uint64_t bit = 1ull << (current_device() & 63);
   if (!(attr_set.load() & bit)) {
