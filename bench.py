@@ -68,7 +68,8 @@ def config(world, global_batch=GLOBAL_BATCH):
         "seq_len": SEQ,
         "parallelism": f"dp{world} (sequences sharded, no data-path collective)",
         "l2": "inputs larger than L2 (x 268 MB + weights 436 MB per pass)",
-        "fusions": "gate/up projections + silu*mul as one tcgen05 GEMM with a SwiGLU epilogue",
+        "fusions": "q/k/v projections + RoPE as one tcgen05 GEMM with a RoPE epilogue; gate/up projections + "
+                   "silu*mul as one tcgen05 GEMM with a SwiGLU epilogue",
     }
 
 
@@ -486,10 +487,11 @@ def main():
         gemm_times = [s.elapsed_time(e) for s, e in gemm_events]
     ms_local = start.elapsed_time(end)
     gemm_ms = sum(gemm_times)
-    # the fused gate/up (SwiGLU) projection is the 5th of the 6 launches of a pass
+    # the fused gate/up (SwiGLU) projection among the GEMM launches of a pass
     shapes = chain.gemm_shapes(tokens)
-    gate_ms = statistics.mean(gemm_times[4::len(shapes)])
-    gm, gn, gk = shapes[4]
+    gi = chain.swiglu_index()
+    gate_ms = statistics.mean(gemm_times[gi::len(shapes)])
+    gm, gn, gk = shapes[gi]
     gate_tflops = 2 * gm * gn * gk / (gate_ms * 1e-3) / 1e12
     ms = max_over_ranks(ms_local, dev)
     value = global_batch * SEQ * args.steps / (ms * 1e-3)
@@ -582,7 +584,7 @@ def main():
             "gpu_launches": launches * world,
             "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (SwiGLU epilogue)",
                          "launch": f"fused gate/up projection [{gm}x{gk}]x[{gk}x{gn}] bf16 -> [{gm}x{gn // 2}] "
-                                   "(largest of the 6 per step)",
+                                   "(largest of the 4 per step)",
                          "achieved": gate_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                          "frac": gate_tflops / peaks["bf16_tflops_sustained"],
                          "traffic": SWIGLU_GEMM_TRAFFIC if batch == GLOBAL_BATCH else None,

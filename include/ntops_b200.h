@@ -195,6 +195,18 @@ NTB_API int ntb_gemm(const NtbTensor* a, const NtbTensor* bm, const NtbTensor* c
  * (torch/silu.py:7-17) and mul (torch/mul.py:7-15). */
 NTB_API int ntb_gemm_swiglu(const NtbTensor* a, const NtbTensor* w, const NtbTensor* d, void* stream);
 
+/* Fused Q / K / V projection with rotary embedding: d = a @ w, then every output head of 128
+ * columns below `rope_cols` is rotated in place, non-interleaved (pairs d, d + 64):
+ * (x0, x1) -> (x0 cos - x1 sin, x0 sin + x1 cos), with the row's position = row % seq_len and
+ * sin / cos tables [seq_len, 64] (contiguous, 16-byte aligned, same dtype).  a: [M, K] (M whole
+ * sequences: rows are (batch, position) flattened), w: [K, N] with N a multiple of 128 (the Q, K
+ * and V weights side by side), d: [M, N]; bf16 or fp16.  The rotation uses the fp32 accumulator
+ * before the output is rounded.  No single reference entry: it fuses mm (torch/mm.py:7-18) with
+ * rotary_position_embedding(..., interleaved=False) (torch/rotary_position_embedding.py:7-29,
+ * kernels/rotary_position_embedding.py:13-15) on the Q and K columns. */
+NTB_API int ntb_gemm_rope(const NtbTensor* a, const NtbTensor* w, const NtbTensor* sin_table,
+                          const NtbTensor* cos_table, const NtbTensor* d, int64_t rope_cols, void* stream);
+
 /* -------------------------------------------------------------- attention ---------------- */
 
 /* Causal variants (kernels/scaled_dot_product_attention.py:12-17): 0 = none. */

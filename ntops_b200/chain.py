@@ -43,9 +43,10 @@ class LayerWeights:
         self.wd = w(FFN, HIDDEN)
         self.norm1 = torch.ones(HIDDEN, device=device, dtype=dtype)
         self.norm2 = torch.ones(HIDDEN, device=device, dtype=dtype)
-        from ntops_b200.fused import pack_swiglu_weight
+        from ntops_b200.fused import pack_qkv_weight, pack_swiglu_weight
 
         self.wgu = pack_swiglu_weight(self.wg, self.wu)  # for the fused SwiGLU projection
+        self.wqkv = pack_qkv_weight(self.wq, self.wk, self.wv)  # for the fused QKV + RoPE projection
 
     def tensors(self):
         return [self.wq, self.wk, self.wv, self.wo, self.wg, self.wu, self.wd, self.norm1, self.norm2]
@@ -59,16 +60,25 @@ def rope_tables(seq_len, device, dtype=torch.bfloat16):
 
 
 def gemm_shapes(tokens, fused=True):
-    """(M, N, K) of the projection launches of one layer pass, in launch order (with ``fused``
-    the gate and up projections are one launch of width 2 * FFN)."""
-    head = [
-        (tokens, HEADS * HEAD_DIM, HIDDEN),
-        (tokens, KV_HEADS * HEAD_DIM, HIDDEN),
-        (tokens, KV_HEADS * HEAD_DIM, HIDDEN),
-        (tokens, HIDDEN, HEADS * HEAD_DIM),
-    ]
+    """(M, N, K) of the projection launches of one layer pass, in launch order.  With ``fused``
+    the Q / K / V projections are one launch (RoPE in its epilogue) and the gate / up
+    projections one launch of width 2 * FFN (SwiGLU in its epilogue)."""
+    if fused:
+        head = [(tokens, (HEADS + 2 * KV_HEADS) * HEAD_DIM, HIDDEN)]
+    else:
+        head = [
+            (tokens, HEADS * HEAD_DIM, HIDDEN),
+            (tokens, KV_HEADS * HEAD_DIM, HIDDEN),
+            (tokens, KV_HEADS * HEAD_DIM, HIDDEN),
+        ]
+    head.append((tokens, HIDDEN, HEADS * HEAD_DIM))
     mlp = [(tokens, 2 * FFN, HIDDEN)] if fused else [(tokens, FFN, HIDDEN), (tokens, FFN, HIDDEN)]
     return head + mlp + [(tokens, HIDDEN, FFN)]
+
+
+def swiglu_index(fused=True):
+    """Position of the fused gate / up (SwiGLU) projection among a pass's GEMM launches."""
+    return 2 if fused else None
 
 
 def layer_flops(batch, seq):
@@ -83,8 +93,9 @@ def layer_flops(batch, seq):
 def layer_forward(x, wts, sin, cos, mm_hook=None, fused=True):
     """One pass of the op chain on x [B, S, 4096] (bf16); returns the down projection [B, S, 4096].
 
-    ``fused`` computes gate / up / silu / mul as one GEMM with a SwiGLU epilogue
-    (``ntops_b200.fused.swiglu_linear``); otherwise each step is its own operator.
+    ``fused`` computes q / k / v and their RoPE as one GEMM with a RoPE epilogue
+    (``ntops_b200.fused.qkv_rope_linear``) and gate / up / silu / mul as one GEMM with a SwiGLU
+    epilogue (``ntops_b200.fused.swiglu_linear``); otherwise each step is its own operator.
     ``mm_hook(fn, a, b)``, when given, wraps every projection call (the benchmark times the
     GEMMs with CUDA events through it)."""
     from ntops_b200 import fused as F
@@ -95,11 +106,22 @@ def layer_forward(x, wts, sin, cos, mm_hook=None, fused=True):
     swiglu = F.swiglu_linear if mm_hook is None else (lambda a, b: mm_hook(F.swiglu_linear, a, b))
     x2 = x.view(T, HIDDEN)
     h = nt.rms_norm(x2, (HIDDEN,), wts.norm1, EPS)
-    q = mm(h, wts.wq).view(B, S, HEADS, HEAD_DIM)
-    k = mm(h, wts.wk).view(B, S, KV_HEADS, HEAD_DIM)
-    v = mm(h, wts.wv).view(B, S, KV_HEADS, HEAD_DIM)
-    q = nt.rotary_position_embedding(q, sin, cos, interleaved=False, inplace=True)
-    k = nt.rotary_position_embedding(k, sin, cos, interleaved=False, inplace=True)
+    if fused:
+        nq, nk = HEADS * HEAD_DIM, KV_HEADS * HEAD_DIM
+
+        def qkv_fn(a, b):
+            return F.qkv_rope_linear(a, b, sin, cos, nq + nk)
+
+        qkv = (qkv_fn(h, wts.wqkv) if mm_hook is None else mm_hook(qkv_fn, h, wts.wqkv)).view(B, S, -1)
+        q = qkv[..., :nq].view(B, S, HEADS, HEAD_DIM)
+        k = qkv[..., nq:nq + nk].view(B, S, KV_HEADS, HEAD_DIM)
+        v = qkv[..., nq + nk:].view(B, S, KV_HEADS, HEAD_DIM)
+    else:
+        q = mm(h, wts.wq).view(B, S, HEADS, HEAD_DIM)
+        k = mm(h, wts.wk).view(B, S, KV_HEADS, HEAD_DIM)
+        v = mm(h, wts.wv).view(B, S, KV_HEADS, HEAD_DIM)
+        q = nt.rotary_position_embedding(q, sin, cos, interleaved=False, inplace=True)
+        k = nt.rotary_position_embedding(k, sin, cos, interleaved=False, inplace=True)
     o = nt.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
                                         enable_gqa=True)
     o2 = o.transpose(1, 2).reshape(T, HEADS * HEAD_DIM)  # a view: o keeps q's [B, S, H, D] layout

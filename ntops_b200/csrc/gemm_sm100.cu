@@ -36,10 +36,14 @@ constexpr int BM = 128;
 constexpr int kRowBytes = 128;  // one swizzle atom row: BK elements of the operand type
 constexpr int kThreads = 192;
 
-// Epilogues: plain (alpha * acc + beta * C), or SwiGLU — the B operand holds gate and up
-// weight columns interleaved in blocks of BN/2, and each tile writes silu(gate) * up.
+// Epilogues: plain (alpha * acc + beta * C); SwiGLU — the B operand holds gate and up weight
+// columns interleaved in blocks of BN/2, and each tile writes silu(gate) * up; RoPE — output
+// columns below rope_cols are heads of 128 whose halves (d, d + 64) are rotated by the row's
+// position (row % rope_seq) with the [rope_seq, 64] sin / cos tables, the rest are plain.
 constexpr int kEpiPlain = 0;
 constexpr int kEpiSwiGLU = 1;
+constexpr int kEpiRope = 2;
+constexpr int kRopeHead = 128;
 
 struct Params {
   int M, N, K, batch;
@@ -52,6 +56,9 @@ struct Params {
   int64_t c_bs, c_ms, c_ns;
   float alpha, beta;
   int n_out;  // SwiGLU epilogue: output columns (= N / 2)
+  const void* rope_sin;  // RoPE epilogue: [rope_seq, 64] tables in the output dtype
+  const void* rope_cos;
+  int rope_cols, rope_seq;
   unsigned int* err;
 };
 
@@ -319,6 +326,56 @@ __global__ void __launch_bounds__(kThreads, 1)
           sm100::tmem_ld_wait();
           const int col0 = nb * (BN / 2) + ch * 32;
           if (row < p.M && col0 < p.n_out) store_swiglu_chunk<TD>(p, drow, col0, g, u);
+        }
+      } else if (EPI == kEpiRope) {
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        const int pos = row % p.rope_seq;
+        const TD* sinr = reinterpret_cast<const TD*>(p.rope_sin) + (int64_t)pos * (kRopeHead / 2);
+        const TD* cosr = reinterpret_cast<const TD*>(p.rope_cos) + (int64_t)pos * (kRopeHead / 2);
+#pragma unroll 1
+        for (int hh = 0; hh < BN / kRopeHead; ++hh) {
+          const int hcol = nb * BN + hh * kRopeHead;  // first column of this head (uniform)
+          if (hcol >= p.N) break;
+          const uint32_t t0 = tmem_base + acc * BN + hh * kRopeHead + lane_off;
+          if (hcol < p.rope_cols) {
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {  // columns d = 32c .. 32c + 31 pair with d + 64
+              uint32_t x1[32], x2[32];
+              sm100::tmem_ld_32x32b_x32(t0 + c * 32, x1);
+              sm100::tmem_ld_32x32b_x32(t0 + 64 + c * 32, x2);
+              sm100::tmem_ld_wait();
+              if (row < p.M) {
+                float o1[32], o2[32];
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                  const ew::Vec<TD, 8> sv = *reinterpret_cast<const ew::Vec<TD, 8>*>(sinr + c * 32 + j);
+                  const ew::Vec<TD, 8> cv = *reinterpret_cast<const ew::Vec<TD, 8>*>(cosr + c * 32 + j);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) {
+                    const float sn = cvt<float>(sv.v[e]), cs = cvt<float>(cv.v[e]);
+                    const float a = __uint_as_float(x1[j + e]), bb = __uint_as_float(x2[j + e]);
+                    o1[j + e] = a * cs - bb * sn;
+                    o2[j + e] = a * sn + bb * cs;
+                  }
+                }
+                store_row_chunk<TD>(p, drow, nullptr, hcol + c * 32, o1);
+                store_row_chunk<TD>(p, drow, nullptr, hcol + 64 + c * 32, o2);
+              }
+            }
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < kRopeHead / 32; ++c) {
+              uint32_t r[32];
+              sm100::tmem_ld_32x32b_x32(t0 + c * 32, r);
+              sm100::tmem_ld_wait();
+              if (row < p.M) {
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                store_row_chunk<TD>(p, drow, nullptr, hcol + c * 32, v);
+              }
+            }
+          }
         }
       } else {
 #pragma unroll 1
@@ -669,4 +726,70 @@ extern "C" int ntb_gemm_swiglu(const NtbTensor* a, const NtbTensor* w, const Ntb
   NTB_UNSUP(tma_operand_ok<__half>(a, oa, p.a_mn, p.M, p.K, 1) && tma_operand_ok<__half>(w, ob, p.b_mn, p.N, p.K, 1),
             "operand rows are not 16-byte aligned for TMA");
   return launch_tc<__half, __half, 256, 4, kEpiSwiGLU>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
+}
+
+extern "C" int ntb_gemm_rope(const NtbTensor* a, const NtbTensor* w, const NtbTensor* sin_table,
+                             const NtbTensor* cos_table, const NtbTensor* d, int64_t rope_cols, void* stream) {
+  using namespace ntb;
+  using namespace ntb::gemm;
+  int rc;
+  if ((rc = check_tensor(a, "input")) != NTB_OK) return rc;
+  if ((rc = check_tensor(w, "weight")) != NTB_OK) return rc;
+  if ((rc = check_tensor(sin_table, "sin_table")) != NTB_OK) return rc;
+  if ((rc = check_tensor(cos_table, "cos_table")) != NTB_OK) return rc;
+  if ((rc = check_tensor(d, "out")) != NTB_OK) return rc;
+  NTB_ARG(a->ndim == 2 && w->ndim == 2 && d->ndim == 2, "rope gemm takes 2-D input, weight and output");
+  NTB_ARG(a->shape[1] == w->shape[0], "inner dimensions differ");
+  NTB_ARG(d->shape[0] == a->shape[0] && d->shape[1] == w->shape[1], "output must be [M, N]");
+  NTB_ARG(d->stride[1] == 1, "output must have a unit column stride");
+  NTB_ARG(sin_table->ndim == 2 && cos_table->ndim == 2 && sin_table->shape[1] == kRopeHead / 2 &&
+              cos_table->shape[1] == kRopeHead / 2 && sin_table->shape[0] == cos_table->shape[0] &&
+              sin_table->shape[0] > 0,
+          "sin / cos tables must be [seq_len, %d]", kRopeHead / 2);
+  NTB_ARG(is_contiguous(sin_table) && is_contiguous(cos_table), "sin / cos tables must be contiguous");
+  NTB_ARG(rope_cols >= 0 && rope_cols % kRopeHead == 0 && rope_cols <= w->shape[1],
+          "rope_cols must be a multiple of %d within the output width", kRopeHead);
+  NTB_ARG(a->shape[0] % sin_table->shape[0] == 0, "rows must be whole sequences of the tables' length");
+  NTB_UNSUP(a->dtype == w->dtype && d->dtype == a->dtype && sin_table->dtype == a->dtype &&
+                cos_table->dtype == a->dtype && (a->dtype == NTB_BF16 || a->dtype == NTB_F16),
+            "rope gemm needs bf16 or fp16 operands, tables and output of one dtype");
+  NTB_UNSUP(reinterpret_cast<uintptr_t>(sin_table->data) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(cos_table->data) % 16 == 0,
+            "sin / cos tables must be 16-byte aligned");
+  Params p = {};
+  p.batch = 1;
+  p.M = (int)a->shape[0];
+  p.K = (int)a->shape[1];
+  p.N = (int)w->shape[1];
+  p.d = d->data;
+  p.d_bs = 0;
+  p.d_ms = d->stride[0];
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  p.rope_sin = sin_table->data;
+  p.rope_cos = cos_table->data;
+  p.rope_cols = (int)rope_cols;
+  p.rope_seq = (int)sin_table->shape[0];
+  p.err = device_error_ptr();
+  if ((int64_t)p.M * p.N == 0) return NTB_OK;
+  NTB_UNSUP(p.K > 0, "K = 0 is not supported by the fused kernel");
+  NTB_UNSUP(p.N % kRopeHead == 0, "output width must be a multiple of %d", kRopeHead);
+  Operand oa{0, a->stride[0], a->stride[1]};
+  Operand ob{0, w->stride[1], w->stride[0]};
+  const bool a_k = oa.s_k == 1 || p.K == 1, a_mn = oa.s_outer == 1 || p.M == 1;
+  const bool b_k = ob.s_k == 1 || p.K == 1, b_mn = ob.s_outer == 1;
+  NTB_UNSUP((a_k || a_mn) && (b_k || b_mn), "operands need a unit stride along K or M / N");
+  p.a_mn = a_k ? 0 : 1;
+  p.b_mn = b_k ? 0 : 1;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a->dtype == NTB_BF16) {
+    NTB_UNSUP(tma_operand_ok<__nv_bfloat16>(a, oa, p.a_mn, p.M, p.K, 1) &&
+                  tma_operand_ok<__nv_bfloat16>(w, ob, p.b_mn, p.N, p.K, 1),
+              "operand rows are not 16-byte aligned for TMA");
+    return launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4, kEpiRope>(a, w, p, oa, ob,
+                                                                      CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
+  }
+  NTB_UNSUP(tma_operand_ok<__half>(a, oa, p.a_mn, p.M, p.K, 1) && tma_operand_ok<__half>(w, ob, p.b_mn, p.N, p.K, 1),
+            "operand rows are not 16-byte aligned for TMA");
+  return launch_tc<__half, __half, 256, 4, kEpiRope>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
 }

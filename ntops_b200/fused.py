@@ -4,6 +4,10 @@
 projections, silu and mul — in one tcgen05 GEMM whose epilogue applies SwiGLU, so the two
 [tokens, 14336] products never reach HBM.  ``pack_swiglu_weight(wg, wu)`` lays the two weights
 out once, interleaved in column blocks of 128, as the kernel expects.
+
+``qkv_rope_linear(x, w_qkv, sin, cos, rope_cols)`` computes the Q, K and V projections as one
+GEMM over the side-by-side weight and rotates the Q and K heads (the first ``rope_cols``
+columns, heads of 128, non-interleaved RoPE) in its epilogue, so RoPE costs no pass over HBM.
 """
 
 import ctypes
@@ -11,7 +15,7 @@ import ctypes
 import torch
 
 from ntops_b200 import _lib
-from ntops_b200.torch.utils import _check_cuda, copy_into, launch, lib
+from ntops_b200.torch.utils import _check_cuda, contiguous, copy_into, launch, lib
 
 BLOCK = 128
 
@@ -40,3 +44,30 @@ def swiglu_linear(x, w_packed, out=None):
     launch("swiglu_linear", lib().ntb_gemm_swiglu, ctypes.byref(xd), ctypes.byref(wd), ctypes.byref(dd),
            device_tensor=d)
     return d
+
+
+def qkv_rope_linear(x, w_qkv, sin_table, cos_table, rope_cols, out=None):
+    """x [M, K] @ w_qkv [K, N], with every 128-column head below ``rope_cols`` rotated by RoPE
+    (non-interleaved; position = row % seq_len of the [seq_len, 64] tables); returns [M, N]."""
+    _check_cuda(x, w_qkv, sin_table, cos_table)
+    M, N = x.shape[0], w_qkv.shape[1]
+    d = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)
+    xd, wd, dd = _lib.describe(x), _lib.describe(w_qkv), _lib.describe(d)
+    sd, cd = _lib.describe(contiguous(sin_table)), _lib.describe(contiguous(cos_table))
+    launch("qkv_rope_linear", lib().ntb_gemm_rope, ctypes.byref(xd), ctypes.byref(wd), ctypes.byref(sd),
+           ctypes.byref(cd), ctypes.byref(dd), int(rope_cols), device_tensor=d)
+    return d
+
+
+def pack_qkv_weight(w_q, w_k, w_v):
+    """[K, Nq], [K, Nk], [K, Nv] -> [K, Nq + Nk + Nv] side by side (Q columns first)."""
+    _check_cuda(w_q, w_k, w_v)
+    K = w_q.shape[0]
+    if not (w_k.shape[0] == K and w_v.shape[0] == K):
+        raise RuntimeError("Q, K and V weights must share their input dimension")
+    nq, nk, nv = w_q.shape[1], w_k.shape[1], w_v.shape[1]
+    packed = torch.empty((K, nq + nk + nv), dtype=w_q.dtype, device=w_q.device)
+    copy_into(packed[:, :nq], w_q)
+    copy_into(packed[:, nq:nq + nk], w_k)
+    copy_into(packed[:, nq + nk:], w_v)
+    return packed

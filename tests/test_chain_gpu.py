@@ -1,5 +1,5 @@
-"""Parity of the fused SwiGLU projection and of the whole Llama layer chain (fused and
-unfused) against the CPU oracle, at a small token count."""
+"""Parity of the fused SwiGLU projection, the fused Q / K / V projection with RoPE, and of the
+whole Llama layer chain (fused and unfused) against the CPU oracle, at a small token count."""
 
 import pytest
 import torch
@@ -28,6 +28,30 @@ def test_swiglu_linear(m, k, n, dtype):
     g64 = x.double() @ wg.double()
     u64 = x.double() @ wu.double()
     want = (g64 / (1 + torch.exp(-g64)) * u64).to(dtype)
+    assert_close(got, want, tol=(2e-2, 2e-2))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("batch,seq,k,heads,kv_heads", [(2, 128, 512, 4, 2), (1, 300, 256, 2, 1), (3, 64, 4096, 3, 1)])
+def test_qkv_rope_linear(batch, seq, k, heads, kv_heads, dtype):
+    from ntops_b200.fused import pack_qkv_weight, qkv_rope_linear
+
+    g = torch.Generator().manual_seed(11)
+    hd = 128
+    x = torch.randn(batch * seq, k, generator=g).to(dtype)
+    wq = (torch.randn(k, heads * hd, generator=g) * 0.05).to(dtype)
+    wk = (torch.randn(k, kv_heads * hd, generator=g) * 0.05).to(dtype)
+    wv = (torch.randn(k, kv_heads * hd, generator=g) * 0.05).to(dtype)
+    sin, cos = O.rope_tables(seq, hd, base=500000.0, dtype=dtype)
+    packed = pack_qkv_weight(wq.to(DEV), wk.to(DEV), wv.to(DEV))
+    assert torch.equal(packed.cpu(), torch.cat((wq, wk, wv), 1))
+    nq, nk = heads * hd, kv_heads * hd
+    got = qkv_rope_linear(x.to(DEV), packed, sin.to(DEV), cos.to(DEV), nq + nk).cpu()
+    # oracle: fp64 products, RoPE on the unrounded q / k (as the epilogue does), one rounding
+    p64 = x.double() @ torch.cat((wq, wk, wv), 1).double()
+    q = O.rotary_position_embedding(p64[:, :nq].view(batch, seq, heads, hd), sin, cos, interleaved=False)
+    kk = O.rotary_position_embedding(p64[:, nq:nq + nk].view(batch, seq, kv_heads, hd), sin, cos, interleaved=False)
+    want = torch.cat((q.reshape(batch * seq, nq), kk.reshape(batch * seq, nk), p64[:, nq + nk:]), 1).to(dtype)
     assert_close(got, want, tol=(2e-2, 2e-2))
 
 
