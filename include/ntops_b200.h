@@ -149,6 +149,14 @@ NTB_API int ntb_clamp_tensor(const NtbTensor* x, const NtbTensor* lo, const NtbT
 NTB_API int ntb_rms_norm(const NtbTensor* x, const NtbTensor* w, const NtbTensor* y, double eps,
                  void* stream);
 
+/* Residual add fused with RMSNorm: s = x + r (rounded to the dtype: the residual stream) and
+ * y = s / sqrt(sum(s^2)/n + eps) * w over each row.  x, r, s, y: 2-D [rows, n] with unit inner
+ * strides and one dtype; w: contiguous [n] or NULL.  s may be x or r (in-place residual update).
+ * No single reference entry: it fuses add (torch/add.py:7-15) and rms_norm
+ * (torch/rms_norm.py:9-31, kernels/rms_norm.py:10-43). */
+NTB_API int ntb_add_rms_norm(const NtbTensor* x, const NtbTensor* r, const NtbTensor* w, const NtbTensor* s,
+                             const NtbTensor* y, double eps, void* stream);
+
 /* LayerNorm: y = (x - mean) / sqrt(var + eps) * w + b, biased variance, fp32 statistics.
  * Same layout rules as ntb_rms_norm; w, b may be NULL.
  * Replaces torch/layer_norm.py:9-33 + kernels/layer_norm.py:11-48. */

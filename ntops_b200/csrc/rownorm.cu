@@ -163,6 +163,91 @@ __global__ void NTB_REG_BOUNDS(NC) rms_norm_reg(const T* __restrict__ x, const T
   if (fail && threadIdx.x == 0 && err != nullptr) atomicOr(err, NTB_DEVERR_TIMEOUT);
 }
 
+// Residual add fused with RMSNorm (register-resident rows): s = x + r rounded to the storage
+// type (the residual stream), y = rms_norm(s) * w computed from the rounded s, as the unfused
+// add then rms_norm would.  The ring brings each chunk of x and of r (second bank) with bulk
+// copies; s and y are written once, so HBM sees two reads and two writes per element instead of
+// three reads and two writes.
+template <typename T, int VEC, int NV, int NC, bool FULL>
+__global__ void NTB_REG_BOUNDS(NC) add_rms_norm_reg(const T* __restrict__ x, const T* __restrict__ r,
+                                                    const T* __restrict__ w, T* __restrict__ s_out,
+                                                    T* __restrict__ y, rs::StreamGeom g, int64_t s_rs,
+                                                    double eps, unsigned int* err) {
+  extern __shared__ __align__(128) uint8_t dyn[];
+  using C = float;
+  using P = float2;
+  using V = ew::Vec<T, VEC>;
+  constexpr int NP = VEC / 2;
+  __shared__ rr::Sum<C> red[32];
+  rs::Ring<T> ring(x, g, dyn);
+  ring.x2 = r;
+  rs::RegRow<T, VEC, NV, NC> rr_;
+  rr_.init(g);
+  ring.start();
+  bool fail = false;
+  for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x) {
+    V sv[NC][NV];  // the rounded sum
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      if (c < g.nchunks && !fail) {
+        const V* sx = reinterpret_cast<const V*>(ring.wait(fail));
+        const V* sr = reinterpret_cast<const V*>(ring.second(reinterpret_cast<const T*>(sx)));
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+          if (FULL || rr_.ok(c, j)) {
+            const V xv = sx[threadIdx.x + j * blockDim.x], rv = sr[threadIdx.x + j * blockDim.x];
+#pragma unroll
+            for (int i = 0; i < NP; ++i) rs::pair_put(sv[c][j], i, rs::p_add(rs::pair_at<C>(xv, i), rs::pair_at<C>(rv, i)));
+          } else {
+            sv[c][j] = V{};
+          }
+        }
+        fail = __syncthreads_or(fail);
+        if (!fail) ring.release(1);
+      } else {
+#pragma unroll
+        for (int j = 0; j < NV; ++j) sv[c][j] = V{};
+      }
+    }
+    if (fail) break;
+    P acc = rs::p_splat(0.f);
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+        if (FULL || rr_.ok(c, j)) {
+          const int vi = c * (g.chunk / VEC) + (int)threadIdx.x + j * (int)blockDim.x;
+          ew::store_cs(reinterpret_cast<V*>(s_out + row * s_rs) + vi, sv[c][j]);
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            const P a = rs::pair_at<C>(sv[c][j], i);
+            acc = rs::p_fma(a, a, acc);
+          }
+        }
+    const C tot = rs::block_reduce_or(rr::Sum<C>{rs::p_hsum(acc)}, red, fail).v;
+    const P rv = rs::p_splat(1.f / sqrtf(tot / (float)g.cols + (float)eps));
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+        if (FULL || rr_.ok(c, j)) {
+          const int vi = c * (g.chunk / VEC) + (int)threadIdx.x + j * (int)blockDim.x;
+          V out;
+          if (w != nullptr) {
+            const V wv = reinterpret_cast<const V*>(w)[vi];
+#pragma unroll
+            for (int i = 0; i < NP; ++i)
+              rs::pair_put(out, i, rs::p_mul(rs::p_mul(rs::pair_at<C>(sv[c][j], i), rv), rs::pair_at<C>(wv, i)));
+          } else {
+#pragma unroll
+            for (int i = 0; i < NP; ++i) rs::pair_put(out, i, rs::p_mul(rs::pair_at<C>(sv[c][j], i), rv));
+          }
+          ew::store_cs(reinterpret_cast<V*>(y + row * g.y_rs) + vi, out);
+        }
+  }
+  if (fail && threadIdx.x == 0 && err != nullptr) atomicOr(err, NTB_DEVERR_TIMEOUT);
+}
+
 // ---------------------------------------------------------------- LayerNorm ---------------
 // Every row is shifted by its first element K (the variance of x - K equals that of x, and K
 // lies within the data, so a mean far from zero neither swamps the sums nor loses the low bits
@@ -492,8 +577,80 @@ int run_norm(bool layer, const NtbTensor* x, const NtbTensor* w, const NtbTensor
   return NTB_OK;
 }
 
+// Fused residual add + rms_norm on the register-resident path; returns NTB_ERR_UNSUPPORTED
+// (without launching) when the rows do not fit it, so the caller can run the two operators.
+template <typename T, int VEC>
+int launch_add_norm(const NtbTensor* x, const NtbTensor* r, const NtbTensor* w, const NtbTensor* s,
+                    const NtbTensor* y, rr::RowGeom g, double eps, cudaStream_t st) {
+  if constexpr (VEC < 2 || std::is_same_v<T, double>) {
+    return NTB_ERR_UNSUPPORTED;
+  } else {
+    rs::RegPlan rp;
+    if (!rs::plan_reg(g.rows, g.cols, g.x_rs, g.y_rs, (int)sizeof(T), VEC, &rp, 16)) return NTB_ERR_UNSUPPORTED;
+    if (!rs::stream_aligned(x->data, g.x_rs, g.rows, (int)sizeof(T)) ||
+        !rs::stream_aligned(r->data, r->stride[0], g.rows, (int)sizeof(T)))
+      return NTB_ERR_UNSUPPORTED;
+    rp.g.banks = 2;
+    rp.g.x2_rs = r->stride[0];
+    // two banks: keep the per-SM ring near the single-tensor budget
+    if (rp.g.slots > 2) rp.g.slots /= 2;
+    const bool full = g.cols == (int64_t)rp.nc_max * rp.threads * rp.nv * VEC && rp.g.chunk == rp.threads * rp.nv * VEC;
+    const auto ring = rs::as_ring_plan(rp);
+    const T* xp = (const T*)x->data;
+    const T* rp_ = (const T*)r->data;
+    const T* wp = w ? (const T*)w->data : nullptr;
+    T* sp = (T*)s->data;
+    T* yp = (T*)y->data;
+    unsigned int* err = device_error_ptr();
+    return rs::dispatch_reg<VEC>(rp, [&](auto nv_, auto nc_) {
+      constexpr int NV = decltype(nv_)::value, NC = decltype(nc_)::value;
+      if constexpr (NV * NC * VEC > 16) {
+        return (int)NTB_ERR_UNSUPPORTED;
+      } else {
+        if (full)
+          return rs::launch_ring(add_rms_norm_reg<T, VEC, NV, NC, true>, ring, (int)sizeof(T), st, xp, rp_, wp, sp, yp,
+                                 rp.g, s->stride[0], eps, err);
+        return rs::launch_ring(add_rms_norm_reg<T, VEC, NV, NC, false>, ring, (int)sizeof(T), st, xp, rp_, wp, sp, yp,
+                               rp.g, s->stride[0], eps, err);
+      }
+    });
+  }
+}
+
+int run_add_norm(const NtbTensor* x, const NtbTensor* r, const NtbTensor* w, const NtbTensor* s,
+                 const NtbTensor* y, double eps, void* stream) {
+  rr::RowGeom g;
+  int rc = check_rows(x, y, w, nullptr, &g);
+  if (rc != NTB_OK) return rc;
+  if ((rc = check_tensor(r, "residual")) != NTB_OK) return rc;
+  if ((rc = check_tensor(s, "sum")) != NTB_OK) return rc;
+  NTB_ARG(r->ndim == 2 && s->ndim == 2 && same_shape(r, x) && same_shape(s, x), "residual and sum must match input");
+  NTB_UNSUP(r->dtype == x->dtype && s->dtype == x->dtype, "residual and sum dtypes must equal the input dtype");
+  NTB_ARG((r->stride[1] == 1 || r->shape[1] == 1) && (s->stride[1] == 1 || s->shape[1] == 1),
+          "residual and sum need a unit inner stride");
+  if (g.rows == 0 || g.cols == 0) return NTB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  rc = NTB_ERR_UNSUPPORTED;
+  NTB_DISPATCH_FLOAT(x->dtype, {
+    constexpr int V = ew::vec_elems<scalar_t>();
+    const int bytes = V * (int)sizeof(scalar_t);
+    if (vec_ok(x, y, w, nullptr, V, g.cols) && ew::aligned(r->data, bytes) && ew::aligned(s->data, bytes) &&
+        (g.rows <= 1 || (r->stride[0] % V == 0 && s->stride[0] % V == 0)))
+      rc = launch_add_norm<scalar_t, V>(x, r, w, s, y, g, eps, st);
+  });
+  if (rc != NTB_ERR_UNSUPPORTED) return rc;
+  // Rows the fused kernel does not take: the two operators.
+  if ((rc = ntb_binary(NTB_BIN_ADD, x, r, s, 1.0, stream)) != NTB_OK) return rc;
+  return run_norm(false, s, w, nullptr, y, eps, stream);
+}
+
 }  // namespace
 }  // namespace ntb
+
+extern "C" int ntb_add_rms_norm(const NtbTensor* x, const NtbTensor* r, const NtbTensor* w, const NtbTensor* s,
+                                const NtbTensor* y, double eps, void* stream) {
+  return ntb::run_add_norm(x, r, w, s, y, eps, stream);
+}
 
 extern "C" int ntb_rms_norm(const NtbTensor* x, const NtbTensor* w, const NtbTensor* y, double eps,
                             void* stream) {

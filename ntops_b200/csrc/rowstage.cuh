@@ -54,6 +54,8 @@ struct StreamGeom {
   int slots;            // ring slots, 2 .. kMaxSlots
   int resident;         // 1: nchunks < slots, a row stays in its slots for all passes
   uint32_t slot_bytes;  // chunk bytes rounded up to 128
+  int banks = 1;        // 2: every load also brings the same chunk of a second tensor
+  int64_t x2_rs = 0;    // row stride of the second tensor
 };
 
 // Producer cursor of a ring, kept in shared memory (only thread 0 touches it) so the other
@@ -65,14 +67,15 @@ struct RingProducer {
   int pitem, pslot;  // load index within the row, slot of the next load
 };
 
-inline size_t ring_smem_bytes(int slots, uint32_t slot_bytes) {
-  return (size_t)slots * slot_bytes + (size_t)kMaxSlots * sizeof(uint64_t) + sizeof(RingProducer);
+inline size_t ring_smem_bytes(int slots, uint32_t slot_bytes, int banks = 1) {
+  return (size_t)banks * slots * slot_bytes + (size_t)kMaxSlots * sizeof(uint64_t) + sizeof(RingProducer);
 }
 
 // The ring of one CTA.  Every thread tracks the consumer side; thread 0 also issues.
 template <typename T>
 struct Ring {
   const T* x;
+  const T* x2 = nullptr;  // second tensor (g.banks == 2): its chunks land in the second bank
   StreamGeom g;
   uint8_t* buf;
   uint64_t* bar;
@@ -82,7 +85,7 @@ struct Ring {
   int row_slot0;      // slot of chunk 0 of the current row (resident mode)
 
   __device__ __forceinline__ Ring(const T* x_, const StreamGeom& g_, uint8_t* dyn)
-      : x(x_), g(g_), buf(dyn), bar(reinterpret_cast<uint64_t*>(dyn + (size_t)g_.slots * g_.slot_bytes)) {
+      : x(x_), g(g_), buf(dyn), bar(reinterpret_cast<uint64_t*>(dyn + (size_t)g_.banks * g_.slots * g_.slot_bytes)) {
     prod = reinterpret_cast<RingProducer*>(bar + kMaxSlots);
     cslot = 0;
     phases = 0u;
@@ -113,8 +116,11 @@ struct Ring {
       const int64_t col0 = (int64_t)c * g.chunk;
       const int64_t n = g.cols - col0 < g.chunk ? g.cols - col0 : g.chunk;
       const uint32_t bytes = (uint32_t)(n * (int64_t)sizeof(T));
-      sm100::mbar_arrive_expect_tx(&bar[p.pslot], bytes);
+      sm100::mbar_arrive_expect_tx(&bar[p.pslot], bytes * (uint32_t)g.banks);
       bulk_load(buf + (size_t)p.pslot * g.slot_bytes, x + p.prow * g.x_rs + col0, bytes, &bar[p.pslot]);
+      if (g.banks == 2)
+        bulk_load(buf + (size_t)(g.slots + p.pslot) * g.slot_bytes, x2 + p.prow * g.x2_rs + col0, bytes,
+                  &bar[p.pslot]);
       ++p.issued;
       if (++p.pslot == g.slots) p.pslot = 0;
       if (++p.pitem == ipr) {
@@ -155,6 +161,11 @@ struct Ring {
   // Frees the oldest k slots.  Call uniformly, right after a CTA barrier that follows the last
   // read of those slots.
   __device__ __forceinline__ void release(int k) { pump(k); }
+
+  // The second tensor's copy of the chunk whose first-bank slot is `p`.
+  __device__ __forceinline__ const T* second(const T* p) const {
+    return reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(p) + (size_t)g.slots * g.slot_bytes);
+  }
 
   __device__ __forceinline__ int chunk_len(int c) const {
     const int64_t col0 = (int64_t)c * g.chunk;
@@ -343,7 +354,7 @@ int blocks_per_sm_smem(const void* kernel, int bt, size_t smem);
 // the second pass reads from L2.
 template <typename Kernel, typename... Args>
 int launch_ring(Kernel kernel, const RingPlan& p, int elem_bytes, cudaStream_t stream, Args... args) {
-  const size_t smem = ring_smem_bytes(p.g.slots, p.g.slot_bytes);
+  const size_t smem = ring_smem_bytes(p.g.slots, p.g.slot_bytes, p.g.banks);
   if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int bpsm = blocks_per_sm_smem(reinterpret_cast<const void*>(kernel), p.threads, smem);
   int per_sm = bpsm < p.ctas_per_sm ? bpsm : p.ctas_per_sm;
@@ -420,14 +431,15 @@ struct RegPlan {
 // registers: a thread holds at most 32 elements (64 registers per thread, 1024 threads per SM).
 // One-chunk rows: a power-of-two block of 32..256 threads, ~128 KB of slots per SM.  Rows of
 // 2..8 chunks: 1024 threads x 1 vector per chunk, one CTA per SM, and a ring of up to 200 KB.
-inline bool plan_reg(int64_t rows, int64_t cols, int64_t x_rs, int64_t y_rs, int es, int vec, RegPlan* p) {
+inline bool plan_reg(int64_t rows, int64_t cols, int64_t x_rs, int64_t y_rs, int es, int vec, RegPlan* p,
+                     int max_elems = 32) {
   int chunk = 0, nc = 0;
   if (!plan_stream(cols, es, vec, &chunk, &nc)) return false;
   const uint32_t slot_bytes = (uint32_t)(((int64_t)chunk * es + 127) / 128 * 128);
   const int nvec = chunk / vec;
   int threads, nv, ncm, k, slots;
   if (nc == 1) {
-    const int max_nv = 32 / vec < 4 ? 32 / vec : 4;
+    const int max_nv = max_elems / vec < 4 ? (max_elems / vec > 0 ? max_elems / vec : 1) : 4;
     threads = 32;
     while (threads < 256 && threads * max_nv < nvec) threads <<= 1;
     nv = 1;
@@ -442,7 +454,7 @@ inline bool plan_reg(int64_t rows, int64_t cols, int64_t x_rs, int64_t y_rs, int
     nv = 1;
     ncm = 2;
     while (ncm < nc) ncm <<= 1;
-    if (nvec > threads || ncm > 8 || ncm * vec > 32) return false;
+    if (nvec > threads || ncm > 8 || ncm * vec > max_elems) return false;
     k = 1;
     slots = (int)(kSmemPerSm / slot_bytes);
   }

@@ -5,6 +5,9 @@ projections, silu and mul — in one tcgen05 GEMM whose epilogue applies SwiGLU,
 [tokens, 14336] products never reach HBM.  ``pack_swiglu_weight(wg, wu)`` lays the two weights
 out once, interleaved in column blocks of 128, as the kernel expects.
 
+``add_rms_norm(x, residual, weight, eps)`` returns ``(s, rms_norm(s))`` with ``s = x + residual``
+in one pass over the rows (the chain's residual add and the following norm).
+
 ``qkv_rope_linear(x, w_qkv, sin, cos, rope_cols)`` computes the Q, K and V projections as one
 GEMM over the side-by-side weight and rotates the Q and K heads (the first ``rope_cols``
 columns, heads of 128, non-interleaved RoPE) in its epilogue, so RoPE costs no pass over HBM.
@@ -71,3 +74,19 @@ def pack_qkv_weight(w_q, w_k, w_v):
     copy_into(packed[:, nq:nq + nk], w_k)
     copy_into(packed[:, nq + nk:], w_v)
     return packed
+
+
+def add_rms_norm(x, residual, weight, eps, out=None):
+    """s = x + residual (rounded to x's dtype) and rms_norm(s) over the last dim with ``weight``;
+    returns ``(s, y)``.  ``out`` may be ``x`` or ``residual`` to update the stream in place."""
+    _check_cuda(x, residual, weight)
+    n = x.shape[-1]
+    x2, r2 = contiguous(x).view(-1, n), contiguous(residual).view(-1, n)
+    s = out if out is not None else torch.empty_like(x2)
+    s2 = s.view(-1, n)
+    y = torch.empty_like(x2)
+    xd, rd, sd, yd = _lib.describe(x2), _lib.describe(r2), _lib.describe(s2), _lib.describe(y)
+    wd = _lib.describe(contiguous(weight).view(n)) if weight is not None else None
+    launch("add_rms_norm", lib().ntb_add_rms_norm, ctypes.byref(xd), ctypes.byref(rd), _lib.ref(wd), ctypes.byref(sd),
+           ctypes.byref(yd), float(eps), device_tensor=y)
+    return s.view(x.shape), y.view(x.shape)

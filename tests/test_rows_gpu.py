@@ -90,6 +90,30 @@ def test_many_rows(rows, cols, dtype):
     assert_close(nt.softmax(xd, -1), O.softmax(x, -1))
 
 
+@pytest.mark.parametrize(
+    "rows,cols,dtype",
+    [(4096, 4096, torch.bfloat16), (777, 4096, torch.float16), (300, 2048, torch.float32), (64, 8192, torch.bfloat16),
+     (50, 33, torch.float32), (1, 16384, torch.bfloat16)],
+)
+@pytest.mark.parametrize("weight_is_none", [False, True])
+def test_add_rms_norm(rows, cols, dtype, weight_is_none):
+    from ntops_b200.fused import add_rms_norm
+
+    x = _randn((rows, cols), dtype)
+    r = _randn((rows, cols), dtype)
+    w = None if weight_is_none else _randn((cols,), dtype)
+    s_want = (x.double() + r.double()).to(dtype)
+    y_want = O.rms_norm(s_want, cols, w, 1e-6)
+    s, y = add_rms_norm(x.to(DEV), r.to(DEV), None if w is None else w.to(DEV), 1e-6)
+    assert torch.equal(s.cpu(), s_want)
+    assert_close(y, y_want)
+    # in place: the sum overwrites x
+    xd = x.to(DEV)
+    s2, y2 = add_rms_norm(xd, r.to(DEV), None if w is None else w.to(DEV), 1e-6, out=xd)
+    assert s2.data_ptr() == xd.data_ptr() and torch.equal(xd.cpu(), s_want)
+    assert_close(y2, y_want)
+
+
 @pytest.mark.parametrize("cols", [4096, 65536])
 def test_layer_norm_offset_data(cols):
     # mean far from zero relative to the spread: the statistics must not cancel
