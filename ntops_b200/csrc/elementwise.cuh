@@ -11,6 +11,8 @@
 //   * strided  — anything else: per-element offset from a coalesced N-d index.
 #pragma once
 
+#include <type_traits>
+
 #include "ntb_common.cuh"
 
 namespace ntb {
@@ -63,24 +65,57 @@ struct Apply;
 template <typename TI, typename TO, typename Op>
 struct Apply<1, TI, TO, Op> {
   using M = typename OpMath<TI>::type;
-  __device__ __forceinline__ static TO run(const Op& op, const TI* x) {
-    return cvt<TO>(op(cvt<M>(x[0])));
-  }
+  __device__ __forceinline__ static auto math(const Op& op, const TI* x) { return op(cvt<M>(x[0])); }
+  __device__ __forceinline__ static TO run(const Op& op, const TI* x) { return cvt<TO>(math(op, x)); }
 };
 template <typename TI, typename TO, typename Op>
 struct Apply<2, TI, TO, Op> {
   using M = typename OpMath<TI>::type;
-  __device__ __forceinline__ static TO run(const Op& op, const TI* x) {
-    return cvt<TO>(op(cvt<M>(x[0]), cvt<M>(x[1])));
-  }
+  __device__ __forceinline__ static auto math(const Op& op, const TI* x) { return op(cvt<M>(x[0]), cvt<M>(x[1])); }
+  __device__ __forceinline__ static TO run(const Op& op, const TI* x) { return cvt<TO>(math(op, x)); }
 };
 template <typename TI, typename TO, typename Op>
 struct Apply<3, TI, TO, Op> {
   using M = typename OpMath<TI>::type;
-  __device__ __forceinline__ static TO run(const Op& op, const TI* x) {
-    return cvt<TO>(op(cvt<M>(x[0]), cvt<M>(x[1]), cvt<M>(x[2])));
-  }
+  __device__ __forceinline__ static auto math(const Op& op, const TI* x) { return op(cvt<M>(x[0]), cvt<M>(x[1]), cvt<M>(x[2])); }
+  __device__ __forceinline__ static TO run(const Op& op, const TI* x) { return cvt<TO>(math(op, x)); }
 };
+
+
+// One output vector from NIN input vectors.  fp32 results bound for fp16 / bf16 are rounded two
+// at a time (one packed conversion per pair, the same round-to-nearest-even as one at a time).
+template <int NIN, typename TI, typename TO, typename Op, int VEC>
+__device__ __forceinline__ Vec<TO, VEC> apply_vec(const Op& op, const Vec<TI, VEC> (&xs)[NIN]) {
+  using A = Apply<NIN, TI, TO, Op>;
+  using R = decltype(A::math(op, static_cast<const TI*>(nullptr)));
+  Vec<TO, VEC> ov;
+  if constexpr (std::is_same_v<R, float> && (std::is_same_v<TO, __nv_bfloat16> || std::is_same_v<TO, __half>) &&
+                VEC % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < VEC; e += 2) {
+      TI a0[NIN], a1[NIN];
+#pragma unroll
+      for (int a = 0; a < NIN; ++a) {
+        a0[a] = xs[a].v[e];
+        a1[a] = xs[a].v[e + 1];
+      }
+      const float r0 = A::math(op, a0), r1 = A::math(op, a1);
+      if constexpr (std::is_same_v<TO, __nv_bfloat16>)
+        *reinterpret_cast<__nv_bfloat162*>(&ov.v[e]) = __floats2bfloat162_rn(r0, r1);
+      else
+        *reinterpret_cast<__half2*>(&ov.v[e]) = __floats2half2_rn(r0, r1);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      TI args[NIN];
+#pragma unroll
+      for (int a = 0; a < NIN; ++a) args[a] = xs[a].v[e];
+      ov.v[e] = A::run(op, args);
+    }
+  }
+  return ov;
+}
 
 template <int NIN>
 struct InPtrs {
@@ -119,15 +154,10 @@ __global__ void __launch_bounds__(kThreads) flat_kernel(Op op, InPtrs<NIN> in, T
     }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      Vec<TO, VEC> ov;
+      Vec<TI, VEC> xu[NIN];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        TI args[NIN];
-#pragma unroll
-        for (int a = 0; a < NIN; ++a) args[a] = xv[a][u].v[e];
-        ov.v[e] = Apply<NIN, TI, TO, Op>::run(op, args);
-      }
-      store_cs(reinterpret_cast<Vec<TO, VEC>*>(out) + v + u * stride, ov);
+      for (int a = 0; a < NIN; ++a) xu[a] = xv[a][u];
+      store_cs(reinterpret_cast<Vec<TO, VEC>*>(out) + v + u * stride, apply_vec<NIN, TI, TO, Op, VEC>(op, xu));
     }
   }
   for (; v < nvec; v += stride) {
@@ -141,15 +171,7 @@ __global__ void __launch_bounds__(kThreads) flat_kernel(Op op, InPtrs<NIN> in, T
         xv[a] = reinterpret_cast<const Vec<TI, VEC>*>(ip[a])[v];
       }
     }
-    Vec<TO, VEC> ov;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      TI args[NIN];
-#pragma unroll
-      for (int a = 0; a < NIN; ++a) args[a] = xv[a].v[e];
-      ov.v[e] = Apply<NIN, TI, TO, Op>::run(op, args);
-    }
-    reinterpret_cast<Vec<TO, VEC>*>(out)[v] = ov;
+    reinterpret_cast<Vec<TO, VEC>*>(out)[v] = apply_vec<NIN, TI, TO, Op, VEC>(op, xv);
   }
   // Scalar tail (n % VEC elements), handled by the first threads of block 0.
   if (blockIdx.x == 0) {
@@ -194,15 +216,7 @@ __global__ void __launch_bounds__(kThreads) rows_kernel(Op op, RowArgs<NIN> in, 
           for (int e = 0; e < VEC; ++e) xv[a].v[e] = s;
         }
       }
-      Vec<TO, VEC> ov;
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        TI args[NIN];
-#pragma unroll
-        for (int a = 0; a < NIN; ++a) args[a] = xv[a].v[e];
-        ov.v[e] = Apply<NIN, TI, TO, Op>::run(op, args);
-      }
-      store_cs(reinterpret_cast<Vec<TO, VEC>*>(op_row) + cv, ov);
+      store_cs(reinterpret_cast<Vec<TO, VEC>*>(op_row) + cv, apply_vec<NIN, TI, TO, Op, VEC>(op, xv));
     }
   }
 }

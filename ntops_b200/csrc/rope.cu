@@ -24,19 +24,21 @@ struct RopeGeom {
 };
 
 // Non-interleaved: chunk c covers x[i .. i+VEC) and x[i+D/2 .. +VEC), i = c*VEC.
-template <typename T, int VEC>
+// IT: index type of the work-item decomposition (32-bit when the item count allows it, so the
+// per-item divisions stay cheap).
+template <typename T, int VEC, typename IT>
 __global__ void __launch_bounds__(256) rope_half(const T* __restrict__ x, const T* __restrict__ sn,
                                                  const T* __restrict__ cs, T* y, RopeGeom g) {
   using C = typename RAcc<T>::type;
   const int64_t half = g.D / 2;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < g.total;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    int64_t r = t / g.chunks;
-    const int64_t c = t - r * g.chunks;
-    const int64_t h = r % g.H;
-    r /= g.H;
-    const int64_t s = r % g.S;
-    const int64_t b = r / g.S;
+  const IT chunks = (IT)g.chunks, H = (IT)g.H, S = (IT)g.S, total = (IT)g.total;
+  for (IT t = (IT)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (IT)gridDim.x * blockDim.x) {
+    IT r = t / chunks;
+    const int64_t c = t - r * chunks;
+    const int64_t h = r % H;
+    r /= H;
+    const int64_t s = r % S;
+    const int64_t b = r / S;
     const int64_t i = c * VEC;
     const T* xp = x + b * g.xs[0] + s * g.xs[1] + h * g.xs[2] + i;
     T* yp = y + b * g.ys[0] + s * g.ys[1] + h * g.ys[2] + i;
@@ -118,11 +120,14 @@ int run_rope(const NtbTensor* x, const NtbTensor* sn, const NtbTensor* cs, const
     if (V > 1 && half % V == 0 && al(V)) {
       g.chunks = half / V;
       g.total = g.B * g.S * g.H * g.chunks;
-      rope_half<T, V><<<grid_for(g.total), 256, 0, st>>>(xp, sp, cp, yp, g);
+      if (g.total < (1ll << 31))
+        rope_half<T, V, uint32_t><<<grid_for(g.total), 256, 0, st>>>(xp, sp, cp, yp, g);
+      else
+        rope_half<T, V, int64_t><<<grid_for(g.total), 256, 0, st>>>(xp, sp, cp, yp, g);
     } else {
       g.chunks = half;
       g.total = g.B * g.S * g.H * g.chunks;
-      rope_half<T, 1><<<grid_for(g.total), 256, 0, st>>>(xp, sp, cp, yp, g);
+      rope_half<T, 1, int64_t><<<grid_for(g.total), 256, 0, st>>>(xp, sp, cp, yp, g);
     }
   } else {
     constexpr int P = V / 2 > 0 ? V / 2 : 1;
