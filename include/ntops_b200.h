@@ -142,6 +142,12 @@ NTB_API int ntb_clamp_tensor(const NtbTensor* x, const NtbTensor* lo, const NtbT
 
 /* ---------------------------------------------------------- row reductions --------------- */
 
+/* Dropout: y = x / (1 - p) where rand(seed, i) > p, else 0, for the element index i of the
+ * contiguous tensors x, y (one floating dtype); rand is the Philox-4x32-10 uniform of the
+ * reference's Triton kernels, so a given seed reproduces the reference's mask.  0 <= p < 1.
+ * Replaces torch/dropout.py:9-29 + kernels/dropout.py:10-11 (the caller draws the seed). */
+NTB_API int ntb_dropout(const NtbTensor* x, const NtbTensor* y, double p, int64_t seed, void* stream);
+
 /* RMSNorm over the last `normalized_numel` elements of each row:
  *   y = x / sqrt(sum(x^2)/n + eps) * w  (fp32 statistics).
  * x, y: 2-D [rows, n] with unit inner stride (row strides free); w: contiguous [n] or NULL.

@@ -59,6 +59,7 @@ EXPORTS = (
     "ntb_gemm_swiglu",
     "ntb_gemm_rope",
     "ntb_add_rms_norm",
+    "ntb_dropout",
     "ntb_sdpa",
     "ntb_sdpa_decode_workspace",
     "ntb_sdpa_decode",
@@ -99,6 +100,7 @@ _SIGNATURES = {
     "ntb_gemm_swiglu": ([_P, _P, _P, _VP], ctypes.c_int),
     "ntb_gemm_rope": ([_P, _P, _P, _P, _P, ctypes.c_int64, _VP], ctypes.c_int),
     "ntb_add_rms_norm": ([_P, _P, _P, _P, _P, ctypes.c_double, _VP], ctypes.c_int),
+    "ntb_dropout": ([_P, _P, ctypes.c_double, ctypes.c_int64, _VP], ctypes.c_int),
     "ntb_sdpa": ([_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP], ctypes.c_int),
     "ntb_sdpa_decode_workspace": ([_P, _P, _P, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "ntb_sdpa_decode": (

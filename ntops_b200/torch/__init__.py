@@ -12,6 +12,7 @@ from ntops_b200.torch.clamp import clamp
 from ntops_b200.torch.copysign import copysign
 from ntops_b200.torch.cos import cos
 from ntops_b200.torch.div import div
+from ntops_b200.torch.dropout import dropout
 from ntops_b200.torch.eq import eq
 from ntops_b200.torch.exp import exp
 from ntops_b200.torch.frac import frac
@@ -57,6 +58,7 @@ __all__ = [
     "copysign",
     "cos",
     "div",
+    "dropout",
     "eq",
     "exp",
     "frac",

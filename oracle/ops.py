@@ -425,3 +425,57 @@ def frac(input):
 def lgamma(input):
     """kernels/lgamma.py:14-29: log |gamma(x)|."""
     return _unary_float(torch.lgamma, input)
+
+
+# ------------------------------------------------------------------------ dropout ---------
+def philox_rand(seed, offsets):
+    """The uniform the reference's dropout draws per element (kernels/dropout.py:10, `ntl.rand`):
+    Triton 3.6's tl.rand (third-party, triton/language/random.py `randint4x` / `philox_impl` /
+    `uint_to_uniform_float`), restated from the published Philox-4x32-10 algorithm (Salmon et
+    al., SC 2011): counter (offset low word, offset high word, 0, 0), key (seed low word, seed
+    high word), 10 rounds with multipliers 0xD2511F53 / 0xCD9E8D57 and key increments 0x9E3779B9 /
+    0xBB67AE85; the first output word x (as int32) maps to (x < 0 ? -x - 1 : x) * 4.6566127342e-10
+    in fp32.  numpy, uint64 arithmetic masked to 32 bits."""
+    import numpy as np
+
+    m = np.uint64(0xFFFFFFFF)
+    off = np.asarray(offsets, dtype=np.int64).astype(np.uint64)
+    c0, c1 = off & m, (off >> np.uint64(32)) & m
+    c2 = np.zeros_like(c0)
+    c3 = np.zeros_like(c0)
+    k0, k1 = np.uint64(seed & 0xFFFFFFFF), np.uint64((seed >> 32) & 0xFFFFFFFF)
+    ra, rb = np.uint64(0xD2511F53), np.uint64(0xCD9E8D57)
+    for _ in range(10):
+        pb, pa = rb * c2, ra * c0
+        c0, c2 = ((pb >> np.uint64(32)) ^ c1 ^ k0) & m, ((pa >> np.uint64(32)) ^ c3 ^ k1) & m
+        c1, c3 = pb & m, pa & m
+        k0, k1 = (k0 + np.uint64(0x9E3779B9)) & m, (k1 + np.uint64(0xBB67AE85)) & m
+    x = c0.astype(np.uint32).view(np.int32).astype(np.int64)
+    x = np.where(x < 0, -x - 1, x)
+    return torch.from_numpy((x.astype(np.float32) * np.float32(4.6566127342e-10)).astype(np.float32))
+
+
+def round_once(t64, dtype):
+    """float64 -> dtype with ONE round-to-nearest-even.  torch's float64 -> float16 / bfloat16
+    conversion on the CPU goes through float32 (two roundings, which differ near midpoints); an
+    intermediate float32 rounded to odd (truncate, then set the last bit when inexact) keeps the
+    second rounding exact, the standard fix for double rounding."""
+    if dtype not in (torch.float16, torch.bfloat16):
+        return t64.to(dtype)
+    r = t64.to(torch.float32)
+    back = r.to(F64)
+    over = back.abs() > t64.abs()
+    trunc = torch.where(over, torch.nextafter(r, torch.zeros_like(r)), r)
+    inexact = trunc.to(F64) != t64
+    bits = trunc.view(torch.int32)
+    odd = torch.where(inexact & torch.isfinite(trunc), bits | 1, bits).view(torch.float32)
+    return odd.to(dtype)
+
+
+def dropout(input, p, seed):
+    """kernels/dropout.py:10-11: where(rand(seed, offset) > p, input / (1 - p), 0) with the
+    element's row-major index as offset; compare and divide in fp64 (p is an fp64 scalar there),
+    one rounding to the output dtype."""
+    r = philox_rand(seed, range(input.numel())).reshape(input.shape).double()
+    y = torch.where(r > p, _f(input) / (1.0 - p), torch.zeros((), dtype=F64))
+    return round_once(y, input.dtype)

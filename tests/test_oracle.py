@@ -177,3 +177,23 @@ def test_planted_oracle_mistake_is_caught():
     for case in cases:
         with pytest.raises(AssertionError):
             assert_close(wrong_rms(*case["inputs"]), case["expected"], tol=(2e-6, 2e-6))
+
+
+def test_philox_oracle_matches_triton_golden():
+    # uniforms of Triton's own tl.rand (the reference dropout's random source), produced by
+    # tests/golden/make_philox_golden.py with Triton's interpreter: the restatement is bit-exact
+    g = torch.load(os.path.join(os.path.dirname(__file__), "golden", "philox_golden.pt"))
+    assert len(g["cases"]) >= 5
+    for c in g["cases"]:
+        got = O.philox_rand(c["seed"], c["offsets"].numpy())
+        assert torch.equal(got, c["rand"]), c["seed"]
+
+
+def test_dropout_oracle_semantics():
+    x = torch.randn(1000, dtype=torch.float64)
+    y = O.dropout(x, 0.3, 42)
+    kept = y != 0
+    assert torch.allclose(y[kept], x[kept] / 0.7)
+    assert 0.6 < kept.double().mean().item() < 0.8
+    r = O.philox_rand(42, range(1000)).double()
+    assert torch.equal(kept, (r > 0.3) & (x != 0))
