@@ -60,6 +60,8 @@ EXPORTS = (
     "ntb_gemm_rope",
     "ntb_add_rms_norm",
     "ntb_dropout",
+    "ntb_conv2d_workspace",
+    "ntb_conv2d",
     "ntb_sdpa",
     "ntb_sdpa_decode_workspace",
     "ntb_sdpa_decode",
@@ -101,6 +103,9 @@ _SIGNATURES = {
     "ntb_gemm_rope": ([_P, _P, _P, _P, _P, ctypes.c_int64, _VP], ctypes.c_int),
     "ntb_add_rms_norm": ([_P, _P, _P, _P, _P, ctypes.c_double, _VP], ctypes.c_int),
     "ntb_dropout": ([_P, _P, ctypes.c_double, ctypes.c_int64, _VP], ctypes.c_int),
+    "ntb_conv2d_workspace": ([_P, _P, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
+    "ntb_conv2d": ([_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _VP, ctypes.c_int64, _VP],
+                   ctypes.c_int),
     "ntb_sdpa": ([_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP], ctypes.c_int),
     "ntb_sdpa_decode_workspace": ([_P, _P, _P, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "ntb_sdpa_decode": (

@@ -9,6 +9,7 @@ from ntops_b200.torch.bitwise_not import bitwise_not
 from ntops_b200.torch.bitwise_or import bitwise_or
 from ntops_b200.torch.bmm import bmm
 from ntops_b200.torch.clamp import clamp
+from ntops_b200.torch.conv2d import conv2d
 from ntops_b200.torch.copysign import copysign
 from ntops_b200.torch.cos import cos
 from ntops_b200.torch.div import div
@@ -55,6 +56,7 @@ __all__ = [
     "bitwise_or",
     "bmm",
     "clamp",
+    "conv2d",
     "copysign",
     "cos",
     "div",

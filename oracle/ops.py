@@ -479,3 +479,15 @@ def dropout(input, p, seed):
     r = philox_rand(seed, range(input.numel())).reshape(input.shape).double()
     y = torch.where(r > p, _f(input) / (1.0 - p), torch.zeros((), dtype=F64))
     return round_once(y, input.dtype)
+
+
+# -------------------------------------------------------------------------- conv2d --------
+def conv2d(input, weight, bias=None, stride=1, padding=0, dilation=1):
+    """kernels/conv2d.py:16-115 (padded input tiled into (C, R, S) patches, mm with the weight
+    flattened to [K, C*R*S], bias in the epilogue; NCHW): computed here in float64 with
+    torch's CPU convolution, the oracle of the reference's tests/test_conv2d.py."""
+    import torch.nn.functional as Fn
+
+    y = Fn.conv2d(_f(input), _f(weight), None if bias is None else _f(bias), stride=stride, padding=padding,
+                  dilation=dilation)
+    return y.to(input.dtype)
