@@ -94,24 +94,6 @@ int sm_count() {
   return cache[dev];
 }
 
-namespace rr {
-int blocks_per_sm(const void* kernel, int bt) {
-  static std::mutex mu;
-  static std::map<std::pair<const void*, int>, int> cache;
-  std::lock_guard<std::mutex> lock(mu);
-  auto key = std::make_pair(kernel, bt);
-  auto it = cache.find(key);
-  if (it != cache.end()) return it->second;
-  int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, bt, 0) != cudaSuccess || n <= 0) {
-    cudaGetLastError();
-    n = 1;
-  }
-  cache[key] = n;
-  return n;
-}
-}  // namespace rr
-
 namespace rs {
 int blocks_per_sm_smem(const void* kernel, int bt, size_t smem) {
   static std::mutex mu;

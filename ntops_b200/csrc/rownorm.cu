@@ -496,7 +496,6 @@ int check_rows(const NtbTensor* x, const NtbTensor* y, const NtbTensor* w, const
   g->cols = x->shape[1];
   g->x_rs = x->stride[0];
   g->y_rs = y->stride[0];
-  g->cs = 1;
   return NTB_OK;
 }
 

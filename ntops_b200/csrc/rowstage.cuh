@@ -195,15 +195,6 @@ struct Max {
   __device__ __forceinline__ Max shfl_xor(int o) const { return {__shfl_xor_sync(0xffffffffu, v, o)}; }
 };
 
-template <typename C>
-struct Sum2 {
-  C a, b;
-  __device__ __forceinline__ static Sum2 combine(const Sum2& x, const Sum2& y) { return {x.a + y.a, x.b + y.b}; }
-  __device__ __forceinline__ Sum2 shfl_xor(int o) const {
-    return {__shfl_xor_sync(0xffffffffu, a, o), __shfl_xor_sync(0xffffffffu, b, o)};
-  }
-};
-
 // ------------------------------------------------------------ element pairs ---------------
 // Statistics and outputs are computed on pairs of adjacent elements: float2 with the sm_100
 // packed fp32 instructions (one instruction per pair, same rounding as the scalar ones), or

@@ -291,7 +291,6 @@ int run_typed(const NtbTensor* x, const NtbTensor* y, int dim, cudaStream_t st) 
     rr::RowGeom g;
     g.rows = outer;
     g.cols = len;
-    g.cs = 1;
     // x and y rows: either both contiguous, or 2-D-expressible with unit inner stride.
     auto row_stride = [&](const NtbTensor* t, int64_t* rs) -> bool {
       if (is_contiguous(t)) {
