@@ -221,9 +221,13 @@ def per_op_table(dev, peaks):
     import ntops_b200.torch as nt
 
     flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    clean_buf = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device=dev)
 
     def flush():
+        # write a buffer larger than L2 (evicts the operator's data), then read another one so the
+        # dirty lines of that write are written back here and not during the timed launch
         flush_buf.fill_(1)
+        clean_buf.amax()
 
     g = torch.Generator(device=dev).manual_seed(0)
     n = 1 << 28

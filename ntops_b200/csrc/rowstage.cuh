@@ -390,23 +390,24 @@ struct RegRow {
   // Copies the next row out of the ring (waiting for each chunk, releasing its slot after a
   // CTA barrier) and returns its first element.  `fail` is uniform on return.
   // Every element of v is assigned (zero where the row has no vector), so no register stays
-  // live from one row to the next.
+  // live from one row to the next.  The row's slots are released together after one CTA
+  // barrier (the ring's other slots keep the next rows' loads in flight meanwhile).
   __device__ __forceinline__ T load(Ring<T>& ring, bool& fail) {
     T first{};
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      if (c < ring.g.nchunks && !fail) {
+      if (c < ring.g.nchunks) {
         const V* s = reinterpret_cast<const V*>(ring.wait(fail));
         if (c == 0) first = reinterpret_cast<const T*>(s)[0];
 #pragma unroll
         for (int j = 0; j < NV; ++j) v[c][j] = ok(c, j) ? s[threadIdx.x + j * blockDim.x] : V{};
-        fail = __syncthreads_or(fail);
-        if (!fail) ring.release(1);
       } else {
 #pragma unroll
         for (int j = 0; j < NV; ++j) v[c][j] = V{};
       }
     }
+    fail = __syncthreads_or(fail);
+    if (!fail) ring.release(ring.g.nchunks);
     return first;
   }
 };
