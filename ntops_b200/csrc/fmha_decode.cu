@@ -209,7 +209,7 @@ struct StreamSmem {
 };
 
 template <typename T, int D, int R>
-__global__ void __launch_bounds__(kStreamThreads) decode_stream(Args a) {
+__global__ void __launch_bounds__(kStreamThreads, R <= 4 ? 3 : 1) decode_stream(Args a) {
   constexpr int LPK = D / 8;          // lanes per key row (one 16-byte vector each)
   constexpr int KPW = 32 / LPK;       // key rows per warp step
   constexpr int U = 8 / KPW;          // steps per block (8 keys of each block per warp)
@@ -305,11 +305,12 @@ __global__ void __launch_bounds__(kStreamThreads) decode_stream(Args a) {
       const int key0 = k_begin + i * kStreamKeys;
       float sc[U][R];
       uint4 vv[U];
+      // partial dot products of all U keys x R rows first, then the butterflies level by level,
+      // so the U * R shuffle chains are independent and interleave
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int kk = warp * 8 + u * KPW + slot;  // key within the block
-        const int key = key0 + kk;
-        const bool valid = key < k_end;
+        const bool valid = key0 + kk < k_end;
         const uint4 kv = *reinterpret_cast<const uint4*>(sk + kk * D * 2 + sub * 16);
         const uint4 vl = *reinterpret_cast<const uint4*>(sv + kk * D * 2 + sub * 16);
         vv[u] = valid ? vl : make_uint4(0, 0, 0, 0);  // rows past the chunk hold stale bytes
@@ -322,11 +323,20 @@ __global__ void __launch_bounds__(kStreamThreads) decode_stream(Args a) {
           float2 d2 = __fmul2_rn(q2[r][0], kf[0]);
 #pragma unroll
           for (int e = 1; e < 4; ++e) d2 = __ffma2_rn(q2[r][e], kf[e], d2);
-          float dot = d2.x + d2.y;
-#pragma unroll
-          for (int o = LPK / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-          sc[u][r] = (valid && key <= kmax[r]) ? dot : -INFINITY;
+          sc[u][r] = d2.x + d2.y;
         }
+      }
+#pragma unroll
+      for (int o = LPK / 2; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int r = 0; r < R; ++r) sc[u][r] += __shfl_xor_sync(0xffffffffu, sc[u][r], o);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int key = key0 + warp * 8 + u * KPW + slot;
+#pragma unroll
+        for (int r = 0; r < R; ++r) sc[u][r] = (key < k_end && key <= kmax[r]) ? sc[u][r] : -INFINITY;
       }
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&empty[st]);  // this warp is done reading the stage
