@@ -415,6 +415,314 @@ __global__ void __launch_bounds__(kStreamThreads, R <= 4 ? 3 : 1) decode_stream(
   }
 }
 
+// Tensor-core split-KV kernel (16-bit K / V, head_dim 64 or 128, up to 16 query rows per kv
+// head, no additive mask).  Same producer / consumer split as decode_stream, with 64-key blocks
+// staged as 8 groups of 8 consecutive keys: one bulk copy per group (one per key when rows are
+// not contiguous in memory), each group followed by 16 bytes of padding.  MMA tile column j
+// of a warp holds key j * 8 + c of the block (slot c of group j): the 8 rows an ldmatrix reads
+// sit one group apart, 16 bytes apart modulo 128, so they fall in different banks.  Warp w
+// takes slots 2w and 2w + 1 of every group (16 keys) and runs the block as m16n8k16 MMAs:
+// S = Q K^T with the (up to 16) query rows as the A operand (held in registers for the whole
+// chunk) and K rows via ldmatrix; online softmax on the S fragments (row max and sum across the
+// 4 lanes sharing a row), P packed to 16 bits straight from the S fragments into the A operand
+// of O += P V, V via ldmatrix.trans.  The tensor cores take the dot products the CUDA-core
+// kernel spends shuffles on.
+constexpr int kMmaKeys = 64;      // keys per stage (16 per consumer warp)
+constexpr int kMmaStages = 3;
+constexpr int kMmaThreads = 160;  // 4 consumer warps + 1 producer warp
+
+template <int D>
+struct MmaSmem {
+  static constexpr int ROW = D * 2;            // one key (bytes)
+  static constexpr int GROUP = 8 * ROW + 16;   // 8 consecutive keys + padding
+  static constexpr int BLOCK = 8 * GROUP;
+  static constexpr int STAGE = 2 * BLOCK;
+  static constexpr int BAR_OFF = kMmaStages * STAGE;
+  static constexpr int TOTAL = BAR_OFF + 2 * kMmaStages * 8 + 16;
+  // the final merge reuses the ring: per warp m[16], l[16], acc[16][D] floats
+  static_assert(4 * (32 + 16 * D) * 4 <= BAR_OFF, "merge buffers must fit the ring");
+  static_assert(GROUP % 128 == 16, "group stride must step 16 bytes through the banks");
+};
+__device__ __forceinline__ int mma_key_off(int kk, int group_bytes, int row_bytes) {
+  return (kk >> 3) * group_bytes + (kk & 7) * row_bytes;
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D (16x8 fp32) += A (16x16) B (16x8), 16-bit operands of type T.
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack16(float lo, float hi) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kMmaThreads) decode_mma(Args a) {
+  using SM = MmaSmem<D>;
+  constexpr int KS = D / 16;  // k-steps of S = Q K^T
+  constexpr int NT = D / 8;   // n-tiles of O
+  extern __shared__ __align__(128) uint8_t dyn[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(dyn + SM::BAR_OFF);
+  uint64_t* empty = full + kMmaStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMmaStages);
+  const int split = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = a.group * a.Sq;
+  const int k_begin = split * a.chunk;
+  const int k_end = min(a.Skv, k_begin + a.chunk);
+  const int nblk = k_end > k_begin ? (k_end - k_begin + kMmaKeys - 1) / kMmaKeys : 0;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kMmaStages; ++st) {
+      sm100::mbar_init(&full[st], 1);
+      sm100::mbar_init(&empty[st], 4);
+    }
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  const int g = lane >> 2, t = lane & 3;  // MMA fragment row group / column pair
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};  // rows g and g + 8
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------- producer ----
+    // lane 0 waits for a free stage and posts the byte count; the 32 lanes then issue the
+    // stage's per-row copies (two per key) side by side
+    const T* Kh = reinterpret_cast<const T*>(a.k) + (int64_t)b * a.k_b + (int64_t)hkv * a.k_h;
+    const T* Vh = reinterpret_cast<const T*>(a.v) + (int64_t)b * a.v_b + (int64_t)hkv * a.v_h;
+    int issued = 0;
+    for (int i = 0; i < nblk; ++i) {
+      const int st = i % kMmaStages;
+      const int key0 = k_begin + i * kMmaKeys;
+      const int nk = min(kMmaKeys, k_end - key0);
+      int ok = 1;
+      if (lane == 0) {
+        if (i >= kMmaStages)
+          ok = sm100::mbar_wait(&empty[st], (uint32_t)(((i / kMmaStages) - 1) & 1), abort_flag, a.err);
+        if (ok) sm100::mbar_arrive_expect_tx(&full[st], 2u * nk * D * 2);
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      uint8_t* sk = dyn + st * SM::STAGE;
+      uint8_t* sv = sk + SM::BLOCK;
+      if (a.k_s == D && a.v_s == D) {
+        // lanes 0-7: K groups, lanes 8-15: V groups
+        const int grp = lane & 7, nkg = min(8, nk - grp * 8);
+        if (lane < 16 && nkg > 0) {
+          if (lane < 8)
+            bulk_g2s(sk + grp * SM::GROUP, Kh + (int64_t)(key0 + grp * 8) * D, nkg * SM::ROW, &full[st]);
+          else
+            bulk_g2s(sv + grp * SM::GROUP, Vh + (int64_t)(key0 + grp * 8) * D, nkg * SM::ROW, &full[st]);
+        }
+      } else {
+        for (int r = lane; r < nk; r += 32) {
+          const int off = mma_key_off(r, SM::GROUP, SM::ROW);
+          bulk_g2s(sk + off, Kh + (int64_t)(key0 + r) * a.k_s, SM::ROW, &full[st]);
+          bulk_g2s(sv + off, Vh + (int64_t)(key0 + r) * a.v_s, SM::ROW, &full[st]);
+        }
+      }
+      ++issued;
+    }
+    if (lane == 0)
+      for (int i = issued - kMmaStages > 0 ? issued - kMmaStages : 0; i < issued; ++i)
+        sm100::mbar_wait_unwind(&full[i % kMmaStages], (uint32_t)((i / kMmaStages) & 1));
+  } else {
+    // ------------------------------------------------------------------ consumers ----
+    const float qs = a.scale * 1.4426950408889634f;  // scores in base-2 units
+    const int off = a.causal == 2 ? a.Skv - a.Sq : 0;
+    int kmax[2];
+    uint32_t qa[KS][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = g + 8 * h;
+      kmax[h] = -1;
+      if (r < rows) kmax[h] = a.causal ? min(a.Skv - 1, r % a.Sq + off) : a.Skv - 1;
+    }
+#pragma unroll
+    for (int kt = 0; kt < KS; ++kt) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {      // rows g (regs 0, 2) and g + 8 (regs 1, 3)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {  // dims kt*16 + 2t (+8)
+          const int r = g + 8 * h, d = kt * 16 + half * 8 + 2 * t;
+          uint32_t v = 0u;
+          if (r < rows) {
+            const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
+            const T* qr = reinterpret_cast<const T*>(a.q) + (int64_t)b * a.q_b + (int64_t)hq * a.q_h +
+                          (int64_t)s * a.q_s + d;
+            v = pack16<T>(cvt<float>(qr[0]), cvt<float>(qr[1]));
+          }
+          qa[kt][h + 2 * half] = v;
+        }
+      }
+    }
+    for (int i = 0; i < nblk; ++i) {
+      const int st = i % kMmaStages;
+      if (!sm100::mbar_wait(&full[st], (uint32_t)((i / kMmaStages) & 1), abort_flag, a.err)) break;
+      uint8_t* sk = dyn + st * SM::STAGE;
+      uint8_t* sv = sk + SM::BLOCK;
+      const int kb = k_begin + i * kMmaKeys;  // first key of the block
+      // this warp's keys: kb + j * 8 + 2 * warp + n for tile column j, n-tile n
+      if (kb + 64 > k_end) {
+        // slots past the chunk hold stale bytes: zero this warp's V rows there (P is 0 for
+        // them, but 0 * NaN would not be)
+        for (int idx = lane; idx < 16 * (D / 8); idx += 32) {
+          const int kk = idx / (D / 8), c = idx % (D / 8);
+          const int key_l = (kk >> 1) * 8 + 2 * warp + (kk & 1);
+          if (kb + key_l >= k_end)
+            *reinterpret_cast<uint4*>(sv + mma_key_off(key_l, SM::GROUP, SM::ROW) + c * 16) = make_uint4(0, 0, 0, 0);
+        }
+        // these generic writes precede any later bulk copy into the stage
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+      }
+      // S = Q K^T for this warp's 16 keys (two n-tiles of 8)
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const int mi = lane >> 3, ri = lane & 7;
+      // matrix mi: n-tile mi >> 1, dims (mi & 1) * 8 .. + 7; row ri = group ri
+      const uint32_t k_base =
+          sm100::smem_u32(sk + ri * SM::GROUP + (2 * warp + (mi >> 1)) * SM::ROW + (mi & 1) * 16);
+#pragma unroll
+      for (int kt = 0; kt < KS; ++kt) {
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(k_base + kt * 32, b00, b01, b10, b11);
+        mma16816<T>(s[0], qa[kt], b00, b01);
+        mma16816<T>(s[1], qa[kt], b10, b11);
+      }
+      // scale, mask, online softmax (rows g: elements 0, 1; row g + 8: elements 2, 3)
+      float mb[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = kb + (2 * t + (e & 1)) * 8 + 2 * warp + n, h = e >> 1;
+          s[n][e] = (key < k_end && key <= kmax[h]) ? s[n][e] * qs : -INFINITY;
+          mb[h] = fmaxf(mb[h], s[n][e]);
+        }
+      float alpha[2], mref[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        mb[h] = fmaxf(mb[h], __shfl_xor_sync(0xffffffffu, mb[h], 1));
+        mb[h] = fmaxf(mb[h], __shfl_xor_sync(0xffffffffu, mb[h], 2));
+        const float m_new = fmaxf(m[h], mb[h]);
+        mref[h] = m_new == -INFINITY ? 0.f : m_new;
+        alpha[h] = sm100::ex2_approx(m[h] - mref[h]);
+        m[h] = m_new;
+        l[h] *= alpha[h];
+      }
+      uint32_t pa[4];
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        float p[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          p[e] = sm100::ex2_approx(s[n][e] - mref[e >> 1]);
+          l[e >> 1] += p[e];
+        }
+        pa[2 * n] = pack16<T>(p[0], p[1]);      // row g, keys 8n + 2t, +1
+        pa[2 * n + 1] = pack16<T>(p[2], p[3]);  // row g + 8
+      }
+      // A fragment order: (row g, k 0-7), (row g+8, k 0-7), (row g, k 8-15), (row g+8, k 8-15)
+      const uint32_t pfrag[4] = {pa[0], pa[1], pa[2], pa[3]};
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        acc[n][0] *= alpha[0];
+        acc[n][1] *= alpha[0];
+        acc[n][2] *= alpha[1];
+        acc[n][3] *= alpha[1];
+      }
+      // O += P V: V rows (keys) via ldmatrix.trans, two n-tiles of 8 dims per load
+      // matrix mi: keys of n-tile mi & 1 (k rows 0-7 / 8-15), dims (mi >> 1) * 8 .. + 7
+      const uint32_t v_base =
+          sm100::smem_u32(sv + ri * SM::GROUP + (2 * warp + (mi & 1)) * SM::ROW + (mi >> 1) * 16);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(v_base + np * 32, b0, b1, b2, b3);
+        mma16816<T>(acc[2 * np], pfrag, b0, b1);
+        mma16816<T>(acc[2 * np + 1], pfrag, b2, b3);
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&empty[st]);  // this warp is done with the stage
+    }
+    // row sums across the 4 lanes of a row
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+      l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+    }
+  }
+  __syncthreads();  // every stage consumed, every copy landed: the ring memory is free
+  if (*abort_flag) return;  // the device error word is already set
+  float* mw = reinterpret_cast<float*>(dyn);        // [4][16]
+  float* lw = mw + 4 * 16;                          // [4][16]
+  float* aw = lw + 4 * 16;                          // [4][16][D]
+  if (warp < 4) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = g + 8 * h;
+      if (t == 0) {
+        mw[warp * 16 + r] = m[h];
+        lw[warp * 16 + r] = l[h];
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+        *reinterpret_cast<float2*>(&aw[(warp * 16 + r) * D + n * 8 + 2 * t]) = make_float2(acc[n][2 * h], acc[n][2 * h + 1]);
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < rows * (D + 2); idx += kMmaThreads) {
+    const int r = idx / (D + 2), d = idx % (D + 2);
+    float M = mw[r];
+#pragma unroll
+    for (int w = 1; w < 4; ++w) M = fmaxf(M, mw[w * 16 + r]);
+    const float Mref = M == -INFINITY ? 0.f : M;
+    float val;
+    if (d == D) {
+      val = M == -INFINITY ? -INFINITY : M * 0.6931471805599453f;  // base 2 -> natural-log units
+    } else {
+      val = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float f = sm100::ex2_approx(mw[w * 16 + r] - Mref);
+        val += (d < D ? aw[(w * 16 + r) * D + d] : lw[w * 16 + r]) * f;
+      }
+    }
+    const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
+    a.ws[((((int64_t)b * a.Hq + hq) * a.Sq + s) * a.splits + split) * (D + 2) + d] = val;
+  }
+}
+
 // One CTA per (batch, q head, query row): merges the chunks' partial results.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) decode_merge(Args a) {
@@ -567,12 +875,22 @@ int launch_stream_d(const Args& a, cudaStream_t st) {
   return launch_stream_r<T, D, 8>(a, st);
 }
 
+template <typename T, int D>
+int launch_mma(const Args& a, cudaStream_t st) {
+  auto k = decode_mma<T, D>;
+  const size_t smem = MmaSmem<D>::TOTAL;
+  if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k<<<dim3(a.splits, a.Hkv, a.B), kMmaThreads, smem, st>>>(a);
+  NTB_LAUNCH_CHECK();
+  return NTB_OK;
+}
+
 template <typename T>
 int launch_typed(const Args& a, cudaStream_t st) {
   if constexpr (!std::is_same_v<T, float>) {
-    if (a.mask == nullptr && a.vec && a.D == a.Dv && (a.D == 64 || a.D == 128) && a.group * a.Sq <= 8 &&
+    if (a.mask == nullptr && a.vec && a.D == a.Dv && (a.D == 64 || a.D == 128) && a.group * a.Sq <= 16 &&
         a.chunk % 32 == 0 && a.Hkv <= 65535 && a.B <= 65535) {
-      const int rc = a.D == 128 ? launch_stream_d<T, 128>(a, st) : launch_stream_d<T, 64>(a, st);
+      const int rc = a.D == 128 ? launch_mma<T, 128>(a, st) : launch_mma<T, 64>(a, st);
       if (rc != NTB_OK) return rc;
       const int64_t rows = (int64_t)a.B * a.Hq * a.Sq;
       NTB_UNSUP(rows <= 0x7fffffffLL, "too many rows");
