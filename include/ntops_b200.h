@@ -252,7 +252,10 @@ NTB_API int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v,
  * against a KV cache) split over the key range for parallelism.  Same tensors and semantics as
  * ntb_sdpa (fp16 / bf16 / fp32, head_dim <= 256, optional additive mask, causal variants);
  * `workspace` is caller-allocated device memory of at least ntb_sdpa_decode_workspace() bytes
- * (16-byte aligned) holding each key chunk's partial output, max and sum.
+ * (16-byte aligned) holding each key chunk's partial output, max and sum.  The common case
+ * (16-bit K / V, head_dim 64 or 128, up to 16 rows per kv head, no mask) merges the chunks on
+ * chip in one launch and leaves the workspace untouched; the size returned covers the other
+ * cases, which a call with a mask takes.
  * Replaces the KV-cache path of torch/scaled_dot_product_attention.py:79-94 +
  * kernels/scaled_dot_product_attention.py:123-151. */
 NTB_API int ntb_sdpa_decode_workspace(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v,
@@ -264,9 +267,11 @@ NTB_API int ntb_sdpa_decode(const NtbTensor* q, const NtbTensor* k, const NtbTen
 /* ntb_sdpa_decode without a workspace argument, for callers that cannot allocate device
  * memory when they run attention (all of HBM already reserved by their own pools, memory that
  * only another allocator hands out, or a foreign-language binding that can pass the tensors it
- * owns but cannot obtain scratch).  The per-chunk partial results live in a fixed 4 MiB device
- * array inside the library, which every GPU that loads the library holds until exit; shapes that
- * need more scratch (ntb_sdpa_decode_workspace() > 4 MiB) are refused with NTB_ERR_UNSUPPORTED.
+ * owns but cannot obtain scratch).  Calls whose key chunks are merged on chip (16-bit K / V,
+ * head_dim 64 or 128, up to 16 GQA group x query rows, no mask) need no scratch; the others keep
+ * their per-chunk partial results in a fixed 4 MiB device array inside the library, which every
+ * GPU that loads the library holds until exit, and are refused with NTB_ERR_UNSUPPORTED when
+ * their partials need more.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
  * that device current; make that first call before any stream capture.  All calls share the
  * array: calls that overlap on the GPU race.  Allocates nothing (no cudaMalloc / cudaFree).

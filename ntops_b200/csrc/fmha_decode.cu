@@ -5,12 +5,19 @@
 // kernels/scaled_dot_product_attention.py:123-151 store the new rows into the cache slots, then
 // run the blockwise online softmax of :154-201 over every key).  With Sq of 1-16 rows the
 // reference's grid has one program per (batch, kv head), far too few to load the cache at HBM
-// speed.  Here the key range is split into chunks: kernel 1 runs one CTA per (batch, kv head,
-// chunk) for the whole GQA group of query rows, staging 32-key K / V tiles through shared
-// memory (fp32, padded rows) and keeping per-row online-softmax state (max, sum, O) in
-// registers; it writes the chunk's unnormalised O and its (max, sum) to a workspace.  Kernel 2
-// merges the chunks: O = sum_c O_c e^(m_c - M) / sum_c l_c e^(m_c - M).  Both are HBM-bound
-// on the K / V bytes.
+// speed.  Here the key range is split into chunks, one CTA per (batch, kv head, chunk) for the
+// whole GQA group of query rows, with per-row online-softmax state (max, sum, O) kept on chip.
+// Two kernels:
+//   decode_mma (16-bit K / V, head_dim 64 / 128, up to 16 rows, no additive mask): tensor-core
+//     MMAs on bulk-copied key blocks; the chunks of a (batch, kv head) form one cluster and merge
+//     through distributed shared memory, so the output is written by the one launch;
+//   decode_partial (every other case: fp32, other head dims, masks, up to 64 rows): CUDA-core
+//     dot products over 32-key tiles staged in fp32; it writes each chunk's unnormalised O and
+//     (max, sum) to a workspace and decode_merge combines the chunks:
+//     O = sum_c O_c e^(m_c - M) / sum_c l_c e^(m_c - M).
+// Both are HBM-bound on the K / V bytes.
+#include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -34,7 +41,8 @@ struct Args {
   int vec;  // K / V rows load as 16-byte vectors
   float scale;
   float* ws;  // [B, Hq, Sq, splits, Dv + 2]: unnormalised O, then max, sum
-  unsigned int* err;  // device error word (bounded waits of decode_stream)
+  unsigned int* err;  // device error word (bounded waits of decode_mma)
+  int mma;            // decode_mma path: chunks merged in-cluster, no workspace
 };
 
 // Bulk global -> shared copy (both addresses 16-byte aligned, bytes a multiple of 16) completing
@@ -57,7 +65,7 @@ template <> __device__ __forceinline__ float2 widen2<__half>(uint32_t w) {
 }
 
 __host__ __device__ inline int64_t ws_floats(const Args& a) {
-  return (int64_t)a.B * a.Hq * a.Sq * a.splits * (a.Dv + 2);
+  return a.mma ? 0 : (int64_t)a.B * a.Hq * a.Sq * a.splits * (a.Dv + 2);
 }
 
 // RPW: query rows per warp (rows r = warp, warp + 4, ...); DC: output columns per lane / 32.
@@ -184,239 +192,9 @@ __global__ void __launch_bounds__(kThreads) decode_partial(Args a) {
   }
 }
 
-// Streaming split-KV kernel for 16-bit K / V with head_dim 64 or 128, at most 8 query rows per
-// kv head and no additive mask (the common decode case).  Warp 4 is a producer: its lane 0
-// streams the CTA's key chunk in blocks of 32 keys through a ring of kStages shared-memory
-// stages with bulk copies (one copy per block of K and of V when a head's rows are contiguous,
-// one per key row otherwise), so ~kStages x 16 KB per CTA are in flight whatever the register
-// budget.  Warps 0-3 consume: each takes 8 keys of every block; a key row is read by D / 8 lanes
-// (16 bytes each, conflict-free), every lane keeps its 8 dimensions of the R query rows
-// (pre-scaled into base-2 units), the running max / sum and its 8 output columns per row in
-// registers; a key's R dot products are finished with a butterfly over its D / 8 lanes and the
-// online-softmax max is shared across the warp so all lanes use one reference.  The 4 consumer
-// warps merge through shared memory into one partial per row (same workspace format as
-// decode_partial: O unnormalised, max in natural-log units, sum).
-constexpr int kStreamKeys = 32;   // keys per stage
-constexpr int kStages = 4;
-constexpr int kStreamThreads = 160;
-
-template <int D>
-struct StreamSmem {
-  static constexpr int BLOCK = kStreamKeys * D * 2;  // bytes of one K (or V) block, 16-bit
-  static constexpr int STAGE = 2 * BLOCK;
-  static constexpr int BAR_OFF = kStages * STAGE;
-  static constexpr int TOTAL = BAR_OFF + 2 * kStages * 8 + 16;
-};
-
-template <typename T, int D, int R>
-__global__ void __launch_bounds__(kStreamThreads, R <= 4 ? 3 : 1) decode_stream(Args a) {
-  constexpr int LPK = D / 8;          // lanes per key row (one 16-byte vector each)
-  constexpr int KPW = 32 / LPK;       // key rows per warp step
-  constexpr int U = 8 / KPW;          // steps per block (8 keys of each block per warp)
-  using SM = StreamSmem<D>;
-  extern __shared__ __align__(128) uint8_t dyn[];
-  __shared__ float sm_m[4][R], sm_l[4][R];
-  __shared__ __align__(16) float sm_acc[4][R][D];
-  uint64_t* full = reinterpret_cast<uint64_t*>(dyn + SM::BAR_OFF);
-  uint64_t* empty = full + kStages;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
-  const int split = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows = a.group * a.Sq;
-  const int k_begin = split * a.chunk;
-  const int k_end = min(a.Skv, k_begin + a.chunk);
-  const int nblk = k_end > k_begin ? (k_end - k_begin + kStreamKeys - 1) / kStreamKeys : 0;
-  if (threadIdx.x == 0) {
-    for (int st = 0; st < kStages; ++st) {
-      sm100::mbar_init(&full[st], 1);
-      sm100::mbar_init(&empty[st], 4);
-    }
-    *abort_flag = 0;
-    sm100::fence_mbar_init();
-  }
-  __syncthreads();
-
-  if (warp == 4) {
-    // ------------------------------------------------------------------- producer ----
-    if (lane == 0) {
-      const T* Kh = reinterpret_cast<const T*>(a.k) + (int64_t)b * a.k_b + (int64_t)hkv * a.k_h;
-      const T* Vh = reinterpret_cast<const T*>(a.v) + (int64_t)b * a.v_b + (int64_t)hkv * a.v_h;
-      int issued = 0;
-      for (int i = 0; i < nblk; ++i) {
-        const int st = i % kStages;
-        if (i >= kStages && !sm100::mbar_wait(&empty[st], (uint32_t)(((i / kStages) - 1) & 1), abort_flag, a.err))
-          break;
-        const int key0 = k_begin + i * kStreamKeys;
-        const int nk = min(kStreamKeys, k_end - key0);
-        const uint32_t row_bytes = D * 2;
-        sm100::mbar_arrive_expect_tx(&full[st], 2u * nk * row_bytes);
-        uint8_t* sk = dyn + st * SM::STAGE;
-        uint8_t* sv = sk + SM::BLOCK;
-        if (a.k_s == D) {
-          bulk_g2s(sk, Kh + (int64_t)key0 * D, nk * row_bytes, &full[st]);
-        } else {
-          for (int r = 0; r < nk; ++r) bulk_g2s(sk + r * row_bytes, Kh + (int64_t)(key0 + r) * a.k_s, row_bytes, &full[st]);
-        }
-        if (a.v_s == D) {
-          bulk_g2s(sv, Vh + (int64_t)key0 * D, nk * row_bytes, &full[st]);
-        } else {
-          for (int r = 0; r < nk; ++r) bulk_g2s(sv + r * row_bytes, Vh + (int64_t)(key0 + r) * a.v_s, row_bytes, &full[st]);
-        }
-        ++issued;
-      }
-      // Leave no copy in flight: wait (bounded) for the last phase of every stage used.
-      for (int i = issued - kStages > 0 ? issued - kStages : 0; i < issued; ++i)
-        sm100::mbar_wait_unwind(&full[i % kStages], (uint32_t)((i / kStages) & 1));
-    }
-  } else {
-    // ------------------------------------------------------------------ consumers ----
-    const int sub = lane % LPK, slot = lane / LPK;
-    const float qs = a.scale * 1.4426950408889634f;  // scores in base-2 units
-    const int off = a.causal == 2 ? a.Skv - a.Sq : 0;
-    float2 q2[R][4];
-    int kmax[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      kmax[r] = -1;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) q2[r][i] = make_float2(0.f, 0.f);
-      if (r < rows) {
-        const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
-        const T* qr = reinterpret_cast<const T*>(a.q) + (int64_t)b * a.q_b + (int64_t)hq * a.q_h + (int64_t)s * a.q_s + sub * 8;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) q2[r][i] = make_float2(cvt<float>(qr[2 * i]) * qs, cvt<float>(qr[2 * i + 1]) * qs);
-        kmax[r] = a.causal ? min(a.Skv - 1, s + off) : a.Skv - 1;
-      }
-    }
-    float m[R], l[R];
-    float2 acc[R][4];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      m[r] = -INFINITY;
-      l[r] = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[r][i] = make_float2(0.f, 0.f);
-    }
-    for (int i = 0; i < nblk; ++i) {
-      const int st = i % kStages;
-      if (!sm100::mbar_wait(&full[st], (uint32_t)((i / kStages) & 1), abort_flag, a.err)) break;
-      const uint8_t* sk = dyn + st * SM::STAGE;
-      const uint8_t* sv = sk + SM::BLOCK;
-      const int key0 = k_begin + i * kStreamKeys;
-      float sc[U][R];
-      uint4 vv[U];
-      // partial dot products of all U keys x R rows first, then the butterflies level by level,
-      // so the U * R shuffle chains are independent and interleave
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int kk = warp * 8 + u * KPW + slot;  // key within the block
-        const bool valid = key0 + kk < k_end;
-        const uint4 kv = *reinterpret_cast<const uint4*>(sk + kk * D * 2 + sub * 16);
-        const uint4 vl = *reinterpret_cast<const uint4*>(sv + kk * D * 2 + sub * 16);
-        vv[u] = valid ? vl : make_uint4(0, 0, 0, 0);  // rows past the chunk hold stale bytes
-        const uint32_t w4[4] = {kv.x, kv.y, kv.z, kv.w};
-        float2 kf[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) kf[e] = widen2<T>(w4[e]);
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          float2 d2 = __fmul2_rn(q2[r][0], kf[0]);
-#pragma unroll
-          for (int e = 1; e < 4; ++e) d2 = __ffma2_rn(q2[r][e], kf[e], d2);
-          sc[u][r] = d2.x + d2.y;
-        }
-      }
-#pragma unroll
-      for (int o = LPK / 2; o > 0; o >>= 1)
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-#pragma unroll
-          for (int r = 0; r < R; ++r) sc[u][r] += __shfl_xor_sync(0xffffffffu, sc[u][r], o);
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int key = key0 + warp * 8 + u * KPW + slot;
-#pragma unroll
-        for (int r = 0; r < R; ++r) sc[u][r] = (key < k_end && key <= kmax[r]) ? sc[u][r] : -INFINITY;
-      }
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&empty[st]);  // this warp is done reading the stage
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        float mb = sc[0][r];
-#pragma unroll
-        for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u][r]);
-#pragma unroll
-        for (int o = LPK; o < 32; o <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-        const float m_new = fmaxf(m[r], mb);
-        const float m_ref = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = sm100::ex2_approx(m[r] - m_ref);
-        m[r] = m_new;
-        float ps = 0.f;
-        float2 pv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) pv[e] = __fmul2_rn(acc[r][e], make_float2(alpha, alpha));
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const float pu = sm100::ex2_approx(sc[u][r] - m_ref);
-          ps += pu;
-          const uint32_t w4[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) pv[e] = __ffma2_rn(make_float2(pu, pu), widen2<T>(w4[e]), pv[e]);
-        }
-        l[r] = l[r] * alpha + ps;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[r][e] = pv[e];
-      }
-    }
-    // Sum the key slots of the warp (every slot shares the warp's reference max).
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-#pragma unroll
-      for (int o = LPK; o < 32; o <<= 1) {
-        l[r] += __shfl_xor_sync(0xffffffffu, l[r], o);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[r][e].x += __shfl_xor_sync(0xffffffffu, acc[r][e].x, o);
-          acc[r][e].y += __shfl_xor_sync(0xffffffffu, acc[r][e].y, o);
-        }
-      }
-      if (slot == 0) {
-        if (sub == 0) {
-          sm_m[warp][r] = m[r];
-          sm_l[warp][r] = l[r];
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) *reinterpret_cast<float2*>(&sm_acc[warp][r][sub * 8 + 2 * e]) = acc[r][e];
-      }
-    }
-  }
-  __syncthreads();
-  if (*abort_flag) return;  // the device error word is already set
-  for (int idx = threadIdx.x; idx < R * (D + 2); idx += kStreamThreads) {
-    const int r = idx / (D + 2), d = idx % (D + 2);
-    if (r >= rows) continue;
-    float M = sm_m[0][r];
-#pragma unroll
-    for (int w = 1; w < 4; ++w) M = fmaxf(M, sm_m[w][r]);
-    const float Mref = M == -INFINITY ? 0.f : M;
-    float val;
-    if (d == D) {
-      val = M == -INFINITY ? -INFINITY : M * 0.6931471805599453f;  // base 2 -> natural-log units
-    } else {
-      val = 0.f;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const float f = sm100::ex2_approx(sm_m[w][r] - Mref);
-        val += (d < D ? sm_acc[w][r][d] : sm_l[w][r]) * f;
-      }
-    }
-    const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
-    a.ws[((((int64_t)b * a.Hq + hq) * a.Sq + s) * a.splits + split) * (D + 2) + d] = val;
-  }
-}
-
 // Tensor-core split-KV kernel (16-bit K / V, head_dim 64 or 128, up to 16 query rows per kv
-// head, no additive mask).  Same producer / consumer split as decode_stream, with 64-key blocks
+// head, no additive mask: the common decode case).  Warp 4 is a producer: it streams the CTA's
+// key chunk through a ring of kMmaStages shared-memory stages with bulk copies, 64-key blocks
 // staged as 8 groups of 8 consecutive keys: one bulk copy per group (one per key when rows are
 // not contiguous in memory), each group followed by 16 bytes of padding.  MMA tile column j
 // of a warp holds key j * 8 + c of the block (slot c of group j): the 8 rows an ldmatrix reads
@@ -425,11 +203,17 @@ __global__ void __launch_bounds__(kStreamThreads, R <= 4 ? 3 : 1) decode_stream(
 // S = Q K^T with the (up to 16) query rows as the A operand (held in registers for the whole
 // chunk) and K rows via ldmatrix; online softmax on the S fragments (row max and sum across the
 // 4 lanes sharing a row), P packed to 16 bits straight from the S fragments into the A operand
-// of O += P V, V via ldmatrix.trans.  The tensor cores take the dot products the CUDA-core
-// kernel spends shuffles on.
+// of O += P V, V via ldmatrix.trans.
+//
+// The chunks of one (batch, kv head) run as one thread-block cluster (a chunk per CTA, at most
+// kMaxCluster): after the key loop each CTA merges its 4 warps' partial results into one per
+// query row in its own shared memory, and after a cluster barrier every CTA finishes a slice
+// of the output rows by reading all chunks' (max, sum, O) through distributed shared memory:
+// O = sum_c O_c 2^(m_c - M) / sum_c l_c 2^(m_c - M).  No workspace and no second launch.
 constexpr int kMmaKeys = 64;      // keys per stage (16 per consumer warp)
 constexpr int kMmaStages = 3;
 constexpr int kMmaThreads = 160;  // 4 consumer warps + 1 producer warp
+constexpr int kMaxCluster = 16;   // chunks per (batch, kv head): CTAs of one cluster
 
 template <int D>
 struct MmaSmem {
@@ -439,9 +223,15 @@ struct MmaSmem {
   static constexpr int STAGE = 2 * BLOCK;
   static constexpr int BAR_OFF = kMmaStages * STAGE;
   static constexpr int TOTAL = BAR_OFF + 2 * kMmaStages * 8 + 16;
-  // the final merge reuses the ring: per warp m[16], l[16], acc[16][D] floats
-  static_assert(4 * (32 + 16 * D) * 4 <= BAR_OFF, "merge buffers must fit the ring");
   static_assert(GROUP % 128 == 16, "group stride must step 16 bytes through the banks");
+  // The merges reuse the ring (bytes): per warp max[16], sum[16] and O[16][AWS] (rows padded
+  // so the fragment stores of 8 rows spread over the banks), then the CTA's max[16], sum[16],
+  // O[16][D] that the cluster reads.
+  static constexpr int AWS = D + 8;
+  static constexpr int MW = 0, LW = 256, AW = 512;
+  static constexpr int CM = AW + 64 * AWS * 4, CL = CM + 64, CA = CL + 64;
+  static_assert(CA + 16 * D * 4 <= BAR_OFF, "merge buffers must fit the ring");
+  static_assert(CA % 16 == 0, "cluster reads of O are 16-byte vectors");
 };
 __device__ __forceinline__ int mma_key_off(int kk, int group_bytes, int row_bytes) {
   return (kk >> 3) * group_bytes + (kk & 7) * row_bytes;
@@ -683,11 +473,16 @@ __global__ void __launch_bounds__(kMmaThreads) decode_mma(Args a) {
     }
   }
   __syncthreads();  // every stage consumed, every copy landed: the ring memory is free
-  if (*abort_flag) return;  // the device error word is already set
-  float* mw = reinterpret_cast<float*>(dyn);        // [4][16]
-  float* lw = mw + 4 * 16;                          // [4][16]
-  float* aw = lw + 4 * 16;                          // [4][16][D]
-  if (warp < 4) {
+  // A CTA whose waits gave up (the device error word is set) skips the merges but still takes
+  // both cluster barriers, which every thread of the cluster must reach.
+  const bool aborted = *abort_flag != 0;
+  float* mw = reinterpret_cast<float*>(dyn + SM::MW);  // [4][16]
+  float* lw = reinterpret_cast<float*>(dyn + SM::LW);  // [4][16]
+  float* aw = reinterpret_cast<float*>(dyn + SM::AW);  // [4][16][AWS]
+  float* cm = reinterpret_cast<float*>(dyn + SM::CM);  // [16] CTA max, base-2 units
+  float* cl = reinterpret_cast<float*>(dyn + SM::CL);  // [16] CTA sum
+  float* ca = reinterpret_cast<float*>(dyn + SM::CA);  // [16][D] CTA unnormalised O
+  if (!aborted && warp < 4) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int r = g + 8 * h;
@@ -697,30 +492,59 @@ __global__ void __launch_bounds__(kMmaThreads) decode_mma(Args a) {
       }
 #pragma unroll
       for (int n = 0; n < NT; ++n)
-        *reinterpret_cast<float2*>(&aw[(warp * 16 + r) * D + n * 8 + 2 * t]) = make_float2(acc[n][2 * h], acc[n][2 * h + 1]);
+        *reinterpret_cast<float2*>(&aw[(warp * 16 + r) * SM::AWS + n * 8 + 2 * t]) =
+            make_float2(acc[n][2 * h], acc[n][2 * h + 1]);
     }
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < rows * (D + 2); idx += kMmaThreads) {
-    const int r = idx / (D + 2), d = idx % (D + 2);
-    float M = mw[r];
+  if (!aborted) {
+    for (int idx = threadIdx.x; idx < rows * (D + 1); idx += kMmaThreads) {
+      const int r = idx / (D + 1), d = idx % (D + 1);
+      float M = mw[r];
 #pragma unroll
-    for (int w = 1; w < 4; ++w) M = fmaxf(M, mw[w * 16 + r]);
-    const float Mref = M == -INFINITY ? 0.f : M;
-    float val;
-    if (d == D) {
-      val = M == -INFINITY ? -INFINITY : M * 0.6931471805599453f;  // base 2 -> natural-log units
-    } else {
-      val = 0.f;
+      for (int w = 1; w < 4; ++w) M = fmaxf(M, mw[w * 16 + r]);
+      const float Mref = M == -INFINITY ? 0.f : M;
+      float val = 0.f;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const float f = sm100::ex2_approx(mw[w * 16 + r] - Mref);
-        val += (d < D ? aw[(w * 16 + r) * D + d] : lw[w * 16 + r]) * f;
+      for (int w = 0; w < 4; ++w)
+        val += (d < D ? aw[(w * 16 + r) * SM::AWS + d] : lw[w * 16 + r]) * sm100::ex2_approx(mw[w * 16 + r] - Mref);
+      if (d < D) {
+        ca[r * D + d] = val;
+      } else {
+        cm[r] = M;
+        cl[r] = val;
       }
     }
-    const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
-    a.ws[((((int64_t)b * a.Hq + hq) * a.Sq + s) * a.splits + split) * (D + 2) + d] = val;
   }
+  sm100::cluster_sync();  // every chunk's result is visible to the whole cluster
+  if (!aborted) {
+    const uint32_t cm_s = sm100::smem_u32(cm), cl_s = sm100::smem_u32(cl), ca_s = sm100::smem_u32(ca);
+    for (int idx = split * kMmaThreads + threadIdx.x; idx < rows * (D / 4); idx += a.splits * kMmaThreads) {
+      const int r = idx / (D / 4), d = (idx % (D / 4)) * 4;
+      float M = -INFINITY;
+      for (int c = 0; c < a.splits; ++c) M = fmaxf(M, sm100::ld_cluster_f32(sm100::cluster_map(cm_s + r * 4, c)));
+      const float Mref = M == -INFINITY ? 0.f : M;
+      float L = 0.f;
+      float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < a.splits; ++c) {
+        const float f = sm100::ex2_approx(sm100::ld_cluster_f32(sm100::cluster_map(cm_s + r * 4, c)) - Mref);
+        L += sm100::ld_cluster_f32(sm100::cluster_map(cl_s + r * 4, c)) * f;
+        const float4 v4 = sm100::ld_cluster_v4(sm100::cluster_map(ca_s + (r * D + d) * 4, c));
+        o4.x += v4.x * f;
+        o4.y += v4.y * f;
+        o4.z += v4.z * f;
+        o4.w += v4.w * f;
+      }
+      const float inv = 1.f / L;  // a fully masked row gives 0 / 0 = NaN, as torch does
+      const int hq = hkv * a.group + r / a.Sq, s = r % a.Sq;
+      T* o = reinterpret_cast<T*>(a.o) + (int64_t)b * a.o_b + (int64_t)hq * a.o_h + (int64_t)s * a.o_s + d;
+      o[0] = cvt<T>(o4.x * inv);
+      o[1] = cvt<T>(o4.y * inv);
+      o[2] = cvt<T>(o4.z * inv);
+      o[3] = cvt<T>(o4.w * inv);
+    }
+  }
+  sm100::cluster_sync();  // no CTA leaves while the cluster still reads its shared memory
 }
 
 // One CTA per (batch, q head, query row): merges the chunks' partial results.
@@ -752,8 +576,47 @@ __global__ void __launch_bounds__(kThreads) decode_merge(Args a) {
 }
 
 // ---------------------------------------------------------------------------- host -------
+// How many clusters of c decode_mma<T, D> CTAs (c = 1..kMaxCluster) the device keeps resident
+// at once (0: not schedulable), asked of the occupancy calculator once per process.  A cluster
+// must fit inside one GPC, so this is not simply the resident CTAs per device / c.
+template <typename T, int D>
+const int* mma_cluster_occupancy() {
+  static std::atomic<int> ready{0};
+  static int occ[kMaxCluster + 1];
+  static std::mutex mu;
+  if (ready.load()) return occ;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ready.load()) return occ;
+  auto k = decode_mma<T, D>;
+  occ[0] = 0;
+  const bool attrs_ok =
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, MmaSmem<D>::TOTAL) == cudaSuccess &&
+      cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  for (int c = 1; c <= kMaxCluster; ++c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c, 1, 1);
+    cfg.blockDim = dim3(kMmaThreads, 1, 1);
+    cfg.dynamicSmemBytes = MmaSmem<D>::TOTAL;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = c;
+    at.val.clusterDim.y = 1;
+    at.val.clusterDim.z = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (!attrs_ok || cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) n = 0;
+    occ[c] = n;
+  }
+  (void)cudaGetLastError();  // a refused query leaves no error behind
+  ready.store(1);
+  return occ;
+}
+
+// allow_mma = false plans the workspace path whatever the inputs (the workspace query, which
+// sees no mask, sizes the workspace for it).
 int plan(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* o, const NtbTensor* mask,
-         double scale, int causal, Args* a) {
+         double scale, int causal, Args* a, bool allow_mma = true) {
   int rc;
   if ((rc = check_tensor(q, "query")) != NTB_OK) return rc;
   if ((rc = check_tensor(k, "key")) != NTB_OK) return rc;
@@ -793,19 +656,6 @@ int plan(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTe
             "attn_mask must be expanded to [B, Hq, Sq, Skv]");
     NTB_UNSUP(mask->dtype == q->dtype, "attn_mask dtype must equal the query dtype");
   }
-  // Split the key range so that (batch x kv heads x chunks) gives about six CTAs per SM (two
-  // waves of the streaming kernel's three resident CTAs), with chunks of at least 256 keys.
-  const int64_t units = (int64_t)a->B * a->Hkv;
-  int splits = (int)((6 * sm_count() + units - 1) / units);
-  const int max_splits = (a->Skv + 255) / 256;
-  if (splits > max_splits) splits = max_splits;
-  if (splits < 1) splits = 1;
-  int chunk = (a->Skv + splits - 1) / splits;
-  chunk = (chunk + kKeys - 1) / kKeys * kKeys;
-  splits = chunk > 0 ? (a->Skv + chunk - 1) / chunk : 1;
-  if (splits < 1) splits = 1;
-  a->splits = splits;
-  a->chunk = chunk > 0 ? chunk : kKeys;
   a->q = q->data;
   a->k = k->data;
   a->v = v->data;
@@ -831,6 +681,40 @@ int plan(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTe
              (a->B == 1 || (a->k_b % ve == 0 && a->v_b % ve == 0)) &&
              reinterpret_cast<uintptr_t>(a->k) % 16 == 0 && reinterpret_cast<uintptr_t>(a->v) % 16 == 0;
   }
+  a->mma = allow_mma && mask == nullptr && a->vec && (q->dtype == NTB_BF16 || q->dtype == NTB_F16) && a->D == a->Dv &&
+           (a->D == 64 || a->D == 128) && a->group * a->Sq <= 16 && a->Hkv <= 65535 && a->B <= 65535;
+  const int64_t units = (int64_t)a->B * a->Hkv;
+  const int max_splits = (a->Skv + 255) / 256;  // chunks of at least 256 keys
+  int splits, step;
+  if (a->mma) {
+    // The most chunks per (batch, kv head) that still keep every cluster resident in one wave
+    // (a second, partial wave costs more than the parallelism gains); one chunk when even
+    // single CTAs take several waves.
+    const int* occ = q->dtype == NTB_BF16
+                         ? (a->D == 128 ? mma_cluster_occupancy<__nv_bfloat16, 128>()
+                                        : mma_cluster_occupancy<__nv_bfloat16, 64>())
+                         : (a->D == 128 ? mma_cluster_occupancy<__half, 128>() : mma_cluster_occupancy<__half, 64>());
+    splits = 1;
+    for (int c = std::min(kMaxCluster, std::max(max_splits, 1)); c >= 1; --c)
+      if (occ[c] >= units) {
+        splits = c;
+        break;
+      }
+    NTB_UNSUP(occ[splits] > 0, "decode attention: the device schedules no cluster of %d CTAs", splits);
+    step = kMmaKeys;
+  } else {
+    // About six CTAs per SM for decode_partial.
+    splits = (int)std::min<int64_t>((6 * sm_count() + units - 1) / units, 1 << 20);
+    step = kKeys;
+  }
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  int chunk = (a->Skv + splits - 1) / splits;
+  chunk = (chunk + step - 1) / step * step;
+  if (chunk <= 0) chunk = step;
+  a->splits = (a->Skv + chunk - 1) / chunk;
+  if (a->splits < 1) a->splits = 1;
+  a->chunk = chunk;
   return NTB_OK;
 }
 
@@ -852,35 +736,24 @@ int launch_dc(const Args& a, size_t smem, cudaStream_t st) {
   return launch_partial<T, RPW, 8>(a, smem, st);
 }
 
-// The streaming kernel serves 16-bit K / V rows readable as 16-byte vectors, head_dim 64 or 128
-// for both K and V, at most 8 query rows per kv head and no additive mask.
-template <typename T, int D, int R>
-int launch_stream_r(const Args& a, cudaStream_t st) {
-  auto k = decode_stream<T, D, R>;
-  const size_t smem = StreamSmem<D>::TOTAL;
-  if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k<<<dim3(a.splits, a.Hkv, a.B), kStreamThreads, smem, st>>>(a);
-  NTB_LAUNCH_CHECK();
-  return NTB_OK;
-}
-
-// The streaming kernel serves 16-bit K / V rows readable as 16-byte vectors, head_dim 64 or 128
-// for both K and V, at most 8 query rows per kv head and no additive mask.
-template <typename T, int D>
-int launch_stream_d(const Args& a, cudaStream_t st) {
-  const int rows = a.group * a.Sq;
-  if (rows <= 1) return launch_stream_r<T, D, 1>(a, st);
-  if (rows <= 2) return launch_stream_r<T, D, 2>(a, st);
-  if (rows <= 4) return launch_stream_r<T, D, 4>(a, st);
-  return launch_stream_r<T, D, 8>(a, st);
-}
-
 template <typename T, int D>
 int launch_mma(const Args& a, cudaStream_t st) {
   auto k = decode_mma<T, D>;
-  const size_t smem = MmaSmem<D>::TOTAL;
-  if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k<<<dim3(a.splits, a.Hkv, a.B), kMmaThreads, smem, st>>>(a);
+  NTB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, MmaSmem<D>::TOTAL));
+  if (a.splits > 8) NTB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, a.Hkv, a.B);
+  cfg.blockDim = dim3(kMmaThreads, 1, 1);
+  cfg.dynamicSmemBytes = MmaSmem<D>::TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = a.splits;  // the chunks of one (batch, kv head)
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  NTB_CUDA(cudaLaunchKernelEx(&cfg, k, a));
   NTB_LAUNCH_CHECK();
   return NTB_OK;
 }
@@ -888,16 +761,7 @@ int launch_mma(const Args& a, cudaStream_t st) {
 template <typename T>
 int launch_typed(const Args& a, cudaStream_t st) {
   if constexpr (!std::is_same_v<T, float>) {
-    if (a.mask == nullptr && a.vec && a.D == a.Dv && (a.D == 64 || a.D == 128) && a.group * a.Sq <= 16 &&
-        a.chunk % 32 == 0 && a.Hkv <= 65535 && a.B <= 65535) {
-      const int rc = a.D == 128 ? launch_mma<T, 128>(a, st) : launch_mma<T, 64>(a, st);
-      if (rc != NTB_OK) return rc;
-      const int64_t rows = (int64_t)a.B * a.Hq * a.Sq;
-      NTB_UNSUP(rows <= 0x7fffffffLL, "too many rows");
-      decode_merge<T><<<(unsigned)rows, kThreads, 0, st>>>(a);
-      NTB_LAUNCH_CHECK();
-      return NTB_OK;
-    }
+    if (a.mma) return a.D == 128 ? launch_mma<T, 128>(a, st) : launch_mma<T, 64>(a, st);
   }
   const size_t smem = sizeof(float) * ((size_t)a.group * a.Sq * a.D + (size_t)kKeys * (a.D + 1) +
                                        (size_t)kKeys * (a.Dv + 1) + 4 * kKeys);
@@ -935,7 +799,9 @@ extern "C" int ntb_sdpa_decode_workspace(const NtbTensor* q, const NtbTensor* k,
   using namespace ntb;
   NTB_ARG(bytes != nullptr, "bytes is NULL");
   decode::Args a;
-  int rc = decode::plan(q, k, v, nullptr, nullptr, 1.0, 0, &a);
+  // sized for the workspace path, which a call with an additive mask takes; calls that take the
+  // cluster-merged path use none of it
+  int rc = decode::plan(q, k, v, nullptr, nullptr, 1.0, 0, &a, false);
   if (rc != NTB_OK) return rc;
   *bytes = decode::ws_floats(a) * (int64_t)sizeof(float);
   return NTB_OK;

@@ -6,7 +6,7 @@ library through a binding that can only pass the tensors it owns).  The test cal
 the C ABI twice in a row, with different shapes, and checks each result against the regular
 entry point ntb_sdpa_decode given a caller-allocated workspace, within the attention tolerance
 the other tests use (2.5e-2 for bf16).  It also checks that shapes needing more than the fixed
-scratch are refused.  This file is collected last so a run that stops at the first failure has
+scratch are refused, and that shapes whose key chunks merge on chip (no scratch) are not.  This file is collected last so a run that stops at the first failure has
 already run every other test.
 """
 
@@ -60,12 +60,22 @@ def test_static_scratch_entry_matches_workspace_entry_twice():
 
 def test_static_scratch_entry_refuses_oversized_shapes():
     L, lib = _lib()
-    # batch 16 x 64 heads x 16 query rows x head_dim 128: ~8.5 MB of partials > 4 MiB
+    # batch 16 x 64 query heads over 32 kv heads x 16 query rows (32 rows per kv head, which
+    # takes the workspace path) x head_dim 128: ~8.5 MB of partials > 4 MiB
     q = torch.zeros((16, 64, 16, 128), dtype=torch.bfloat16, device="cuda")
-    k = torch.zeros((16, 64, 256, 128), dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros((16, 32, 256, 128), dtype=torch.bfloat16, device="cuda")
     o = torch.empty_like(q)
     qd, kd, od = L.describe(q), L.describe(k), L.describe(o)
     rc = lib.ntb_sdpa_decode_static(ctypes.byref(qd), ctypes.byref(kd), ctypes.byref(kd), None, ctypes.byref(od),
                                     0.1, 0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == L.ERR_UNSUPPORTED
     assert b"static scratch" in lib.ntb_last_error()
+
+
+def test_static_scratch_entry_takes_large_cluster_merged_shapes():
+    L, lib = _lib()
+    # 16 rows per kv head, bf16, head_dim 128: the chunks merge on chip and need no scratch, so
+    # a shape whose partials would not fit the 4 MiB array still runs
+    o_static, o_ref = _run_both(L, lib, 16, 64, 64, 16, 256, 128, 0, 3)
+    assert torch.isfinite(o_static.float()).all()
+    torch.testing.assert_close(o_static.float(), o_ref.float(), rtol=2.5e-2, atol=2.5e-2)
