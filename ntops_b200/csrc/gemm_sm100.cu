@@ -147,6 +147,94 @@ __device__ __forceinline__ void store_swiglu_chunk(const Params& p, TD* drow, in
   }
 }
 
+// Epilogue of one output tile for the 4 epilogue warps: TMEM accumulator columns tacc ..
+// tacc + BN - 1 hold this CTA's 128 rows of the tile; the calling thread owns TMEM lane
+// q * 32 + lane, output row `row` (batch b), and the tile's N-block is nb.
+template <typename TD, int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, int q, int lane, int b, int row,
+                                              int nb) {
+  TD* drow = reinterpret_cast<TD*>(p.d) + (int64_t)b * p.d_bs + (int64_t)row * p.d_ms;
+  const TD* crow = nullptr;
+  if (p.c != nullptr && p.beta != 0.f)
+    crow = reinterpret_cast<const TD*>(p.c) + (int64_t)b * p.c_bs + (int64_t)row * p.c_ms;
+  if (EPI == kEpiSwiGLU) {
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 64; ++ch) {
+      uint32_t g[32], u[32];
+      const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+      sm100::tmem_ld_32x32b_x32(tacc + ch * 32 + lane_off, g);
+      sm100::tmem_ld_32x32b_x32(tacc + BN / 2 + ch * 32 + lane_off, u);
+      sm100::tmem_ld_wait();
+      const int col0 = nb * (BN / 2) + ch * 32;
+      if (row < p.M && col0 < p.n_out) store_swiglu_chunk<TD>(p, drow, col0, g, u);
+    }
+  } else if (EPI == kEpiRope) {
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const int pos = row % p.rope_seq;
+    const TD* sinr = reinterpret_cast<const TD*>(p.rope_sin) + (int64_t)pos * (kRopeHead / 2);
+    const TD* cosr = reinterpret_cast<const TD*>(p.rope_cos) + (int64_t)pos * (kRopeHead / 2);
+#pragma unroll 1
+    for (int hh = 0; hh < BN / kRopeHead; ++hh) {
+      const int hcol = nb * BN + hh * kRopeHead;  // first column of this head (uniform)
+      if (hcol >= p.N) break;
+      const uint32_t t0 = tacc + hh * kRopeHead + lane_off;
+      if (hcol < p.rope_cols) {
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {  // columns d = 32c .. 32c + 31 pair with d + 64
+          uint32_t x1[32], x2[32];
+          sm100::tmem_ld_32x32b_x32(t0 + c * 32, x1);
+          sm100::tmem_ld_32x32b_x32(t0 + 64 + c * 32, x2);
+          sm100::tmem_ld_wait();
+          if (row < p.M) {
+            float o1[32], o2[32];
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              const ew::Vec<TD, 8> sv = *reinterpret_cast<const ew::Vec<TD, 8>*>(sinr + c * 32 + j);
+              const ew::Vec<TD, 8> cv = *reinterpret_cast<const ew::Vec<TD, 8>*>(cosr + c * 32 + j);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float sn = cvt<float>(sv.v[e]), cs = cvt<float>(cv.v[e]);
+                const float a = __uint_as_float(x1[j + e]), bb = __uint_as_float(x2[j + e]);
+                o1[j + e] = a * cs - bb * sn;
+                o2[j + e] = a * sn + bb * cs;
+              }
+            }
+            store_row_chunk<TD>(p, drow, nullptr, hcol + c * 32, o1);
+            store_row_chunk<TD>(p, drow, nullptr, hcol + 64 + c * 32, o2);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kRopeHead / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld_32x32b_x32(t0 + c * 32, r);
+          sm100::tmem_ld_wait();
+          if (row < p.M) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            store_row_chunk<TD>(p, drow, nullptr, hcol + c * 32, v);
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 32; ++ch) {
+      uint32_t r[32];
+      sm100::tmem_ld_32x32b_x32(tacc + ch * 32 + ((uint32_t)(q * 32) << 16), r);
+      sm100::tmem_ld_wait();
+      const int col0 = nb * BN + ch * 32;
+      if (row < p.M && col0 < p.N) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        store_row_chunk<TD>(p, drow, crow, col0, v);
+      }
+    }
+  }
+}
+
 // T: operand element type (__half / __nv_bfloat16 / float for TF32); TD: output type.
 template <typename T, typename TD, int BN, int STAGES, int EPI = kEpiPlain>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -311,87 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(tile, p, b, mb, nb);
       if (!sm100::mbar_wait(&tmem_full[acc], acc_phase, abort_flag, p.err)) break;
       sm100::tc_fence_after();
-      const int row = mb * BM + row_in_tile;
-      TD* drow = reinterpret_cast<TD*>(p.d) + (int64_t)b * p.d_bs + (int64_t)row * p.d_ms;
-      const TD* crow = nullptr;
-      if (p.c != nullptr && p.beta != 0.f)
-        crow = reinterpret_cast<const TD*>(p.c) + (int64_t)b * p.c_bs + (int64_t)row * p.c_ms;
-      if (EPI == kEpiSwiGLU) {
-#pragma unroll 1
-        for (int ch = 0; ch < BN / 64; ++ch) {
-          uint32_t g[32], u[32];
-          const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-          sm100::tmem_ld_32x32b_x32(tmem_base + acc * BN + ch * 32 + lane_off, g);
-          sm100::tmem_ld_32x32b_x32(tmem_base + acc * BN + BN / 2 + ch * 32 + lane_off, u);
-          sm100::tmem_ld_wait();
-          const int col0 = nb * (BN / 2) + ch * 32;
-          if (row < p.M && col0 < p.n_out) store_swiglu_chunk<TD>(p, drow, col0, g, u);
-        }
-      } else if (EPI == kEpiRope) {
-        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        const int pos = row % p.rope_seq;
-        const TD* sinr = reinterpret_cast<const TD*>(p.rope_sin) + (int64_t)pos * (kRopeHead / 2);
-        const TD* cosr = reinterpret_cast<const TD*>(p.rope_cos) + (int64_t)pos * (kRopeHead / 2);
-#pragma unroll 1
-        for (int hh = 0; hh < BN / kRopeHead; ++hh) {
-          const int hcol = nb * BN + hh * kRopeHead;  // first column of this head (uniform)
-          if (hcol >= p.N) break;
-          const uint32_t t0 = tmem_base + acc * BN + hh * kRopeHead + lane_off;
-          if (hcol < p.rope_cols) {
-#pragma unroll 1
-            for (int c = 0; c < 2; ++c) {  // columns d = 32c .. 32c + 31 pair with d + 64
-              uint32_t x1[32], x2[32];
-              sm100::tmem_ld_32x32b_x32(t0 + c * 32, x1);
-              sm100::tmem_ld_32x32b_x32(t0 + 64 + c * 32, x2);
-              sm100::tmem_ld_wait();
-              if (row < p.M) {
-                float o1[32], o2[32];
-#pragma unroll
-                for (int j = 0; j < 32; j += 8) {
-                  const ew::Vec<TD, 8> sv = *reinterpret_cast<const ew::Vec<TD, 8>*>(sinr + c * 32 + j);
-                  const ew::Vec<TD, 8> cv = *reinterpret_cast<const ew::Vec<TD, 8>*>(cosr + c * 32 + j);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) {
-                    const float sn = cvt<float>(sv.v[e]), cs = cvt<float>(cv.v[e]);
-                    const float a = __uint_as_float(x1[j + e]), bb = __uint_as_float(x2[j + e]);
-                    o1[j + e] = a * cs - bb * sn;
-                    o2[j + e] = a * sn + bb * cs;
-                  }
-                }
-                store_row_chunk<TD>(p, drow, nullptr, hcol + c * 32, o1);
-                store_row_chunk<TD>(p, drow, nullptr, hcol + 64 + c * 32, o2);
-              }
-            }
-          } else {
-#pragma unroll 1
-            for (int c = 0; c < kRopeHead / 32; ++c) {
-              uint32_t r[32];
-              sm100::tmem_ld_32x32b_x32(t0 + c * 32, r);
-              sm100::tmem_ld_wait();
-              if (row < p.M) {
-                float v[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                store_row_chunk<TD>(p, drow, nullptr, hcol + c * 32, v);
-              }
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int ch = 0; ch < BN / 32; ++ch) {
-          uint32_t r[32];
-          sm100::tmem_ld_32x32b_x32(tmem_base + acc * BN + ch * 32 + ((uint32_t)(q * 32) << 16), r);
-          sm100::tmem_ld_wait();
-          const int col0 = nb * BN + ch * 32;
-          if (row < p.M && col0 < p.N) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            store_row_chunk<TD>(p, drow, crow, col0, v);
-          }
-        }
-      }
+      epilogue_tile<TD, BN, EPI>(p, tmem_base + acc * BN, q, lane, b, mb * BM + row_in_tile, nb);
       sm100::tc_fence_before();
       sm100::mbar_arrive(&tmem_empty[acc]);
       acc ^= 1;
@@ -403,6 +411,236 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------- CTA-pair kernel ------
+// 16-bit operands, tiles of 256 x 256 computed by a cluster of two CTAs on two SMs with
+// cta_group::2 MMAs (M = 256, N = 256): CTA r of the pair stages rows r * 128 .. + 127 of the
+// A block and columns r * 128 .. + 127 of the B block (32 KB per stage instead of the 48 KB a
+// single-SM 128 x 256 tile needs), and its TMEM receives its 128 rows over all 256 columns, so
+// each SM pulls a third less operand data from L2 per FLOP and the smaller stages buy a
+// 6-deep ring.  Roles as in gemm_tc_kernel:
+//   * warp 0 of each CTA loads its halves; the loads complete on the leader's (rank 0) full
+//     barrier, which the leader arms with both CTAs' bytes;
+//   * warp 1 of the leader issues the MMAs and commits each stage to both CTAs' empty barriers
+//     and each finished accumulator to both CTAs' tmem_full barriers;
+//   * warps 2-5 of each CTA drain its own TMEM half and arrive (one arrival per warp) on the
+//     leader's tmem_empty barrier.
+// TMEM (2 x 256 columns, double-buffered) is allocated and freed by warp 1 of both CTAs
+// together.
+template <int STAGES>
+struct PairSmem {
+  static constexpr int A_BYTES = BM * kRowBytes;         // 16 KB: this CTA's 128 A rows
+  static constexpr int B_BYTES = 128 * kRowBytes;        // 16 KB: this CTA's 128 B columns
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = TILE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
+};
+constexpr int kPairBM = 256;  // rows per pair tile
+constexpr int kPairBN = 256;  // columns per pair tile (the MMA's N)
+
+template <typename T, typename TD, int STAGES, int EPI = kEpiPlain>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                        Params p) {
+  static_assert(sizeof(T) == 2, "the CTA-pair kernel takes 16-bit operands");
+  using S = PairSmem<STAGES>;
+  constexpr int BN = kPairBN;
+  constexpr int BK = kRowBytes / 2;
+  constexpr int UMMA_K = 16;
+  constexpr int KSTEPS = BK / UMMA_K;
+  constexpr uint32_t kFormat = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr int TMEM_COLS = 2 * BN;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILE_BYTES);  // used in the leader
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;  // used in the leader
+  uint64_t* done_bar = tmem_empty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = sm100::cluster_ctarank();  // 0: leader, 1: peer
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tmem_full[a], 1);
+      sm100::mbar_init(&tmem_empty[a], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    sm100::mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+    sm100::tma_prefetch_desc(&tma_a);
+    sm100::tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc_pair(tmem_base_slot, TMEM_COLS);
+    sm100::tmem_relinquish_pair();
+  }
+  sm100::tc_fence_before();
+  sm100::cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer ----
+    if (lane == 0) {
+      const uint32_t full_leader = sm100::cluster_map(sm100::smem_u32(full), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;        // bit s: stage s was armed at least once (leader)
+      uint32_t last_parity = 0;  // bit s: parity of stage s's last armed phase
+      bool ok = true;
+      for (int tile = pair; ok && tile < p.tiles; tile += npairs) {
+        int b, mb, nb;
+        tile_coords(tile, p, b, mb, nb);
+        const int row0 = mb * kPairBM + (int)rank * BM;
+        const int col0 = nb * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!sm100::mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) {
+            sm100::mbar_arrive_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
+            armed |= 1u << stage;
+            last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          }
+          const uint32_t bar = full_leader + stage * 8;
+          uint8_t* a_dst = sA + stage * S::A_BYTES;
+          uint8_t* b_dst = sB + stage * S::B_BYTES;
+          if (!p.a_mn) {
+            sm100::tma_load_3d_pair(a_dst, &tma_a, bar, kb * BK, row0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              sm100::tma_load_3d_pair(a_dst + j * BK * kRowBytes, &tma_a, bar, row0 + j * 64, kb * BK, b);
+          }
+          if (!p.b_mn) {
+            sm100::tma_load_3d_pair(b_dst, &tma_b, bar, kb * BK, col0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < (BN / 2) / 64; ++j)
+              sm100::tma_load_3d_pair(b_dst + j * BK * kRowBytes, &tma_b, bar, col0 + j * 64, kb * BK, b);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Unwind: every load of the pair must land before either CTA may exit.  The leader's
+      // full barriers count both CTAs' bytes, so the leader waits for its armed phases.
+      if (rank == 0)
+        for (int s = 0; s < STAGES; ++s)
+          if (armed & (1u << s)) sm100::mbar_wait_unwind(&full[s], (last_parity >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader) ----
+    if (rank == 0) {
+      constexpr uint32_t idesc_kk = sm100::instr_desc(kFormat, false, false, kPairBM, BN);
+      const uint32_t idesc = idesc_kk | ((p.a_mn ? 1u : 0u) << 15) | ((p.b_mn ? 1u : 0u) << 16);
+      const uint32_t a_kstep = p.a_mn ? UMMA_K * kRowBytes : UMMA_K * 2u;
+      const uint32_t b_kstep = p.b_mn ? UMMA_K * kRowBytes : UMMA_K * 2u;
+      const uint32_t a_lbo = p.a_mn ? BK * kRowBytes : 16, a_sbo = 1024;
+      const uint32_t b_lbo = p.b_mn ? BK * kRowBytes : 16, b_sbo = 1024;
+      const uint32_t empty_self = sm100::smem_u32(empty), empty_peer = sm100::cluster_map(empty_self, 1);
+      const uint32_t tfull_self = sm100::smem_u32(tmem_full), tfull_peer = sm100::cluster_map(tfull_self, 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < p.tiles; tile += npairs) {
+        if (!sm100::mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!sm100::mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          if (lane == 0) {
+            const uint32_t a0 = sm100::smem_u32(sA + stage * S::A_BYTES);
+            const uint32_t b0 = sm100::smem_u32(sB + stage * S::B_BYTES);
+#pragma unroll
+            for (int k = 0; k < KSTEPS; ++k) {
+              const uint64_t ad = sm100::smem_desc(a0 + k * a_kstep, a_lbo, a_sbo);
+              const uint64_t bd = sm100::smem_desc(b0 + k * b_kstep, b_lbo, b_sbo);
+              sm100::mma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            }
+            sm100::mma_commit_pair(empty_self + stage * 8);
+            sm100::mma_commit_pair(empty_peer + stage * 8);
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if (lane == 0) {
+          sm100::mma_commit_pair(tfull_self + acc * 8);
+          sm100::mma_commit_pair(tfull_peer + acc * 8);
+        }
+        __syncwarp();
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Unwind: wait until every MMA issued by this warp has completed.
+      if (lane == 0) {
+        sm100::mma_commit_pair(sm100::smem_u32(done_bar));
+        sm100::mbar_wait_unwind(done_bar, 0);
+      }
+      __syncwarp();
+    }
+  } else {
+    // -------------------------------------------------------------------- epilogue ----
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t tempty_leader = sm100::cluster_map(sm100::smem_u32(tmem_empty), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < p.tiles; tile += npairs) {
+      int b, mb, nb;
+      tile_coords(tile, p, b, mb, nb);
+      if (!sm100::mbar_wait(&tmem_full[acc], acc_phase, abort_flag, p.err)) break;
+      sm100::tc_fence_after();
+      epilogue_tile<TD, BN, EPI>(p, tmem_base + acc * BN, q, lane, b, mb * kPairBM + (int)rank * BM + q * 32 + lane,
+                                 nb);
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive_cluster(tempty_leader + acc * 8);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  // A CTA that gave up may still have loads in flight that the leader never armed for (their
+  // bytes complete on no armed phase): give them time to land before the pair's memory goes.
+  if (*abort_flag) {
+    const uint64_t t0 = sm100::globaltimer();
+    while (sm100::globaltimer() - t0 < 200000ull) {
+    }
+  }
+  __syncwarp();
+  sm100::tc_fence_before();
+  sm100::cluster_sync();  // no CTA leaves while the pair still reads its memory or TMEM
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -517,6 +755,93 @@ int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& 
   kernel<<<grid, kThreads, S::TOTAL, st>>>(ta, tb, p);
   NTB_LAUNCH_CHECK();
   return NTB_OK;
+}
+
+// Pairs of CTAs the device keeps resident for gemm_tc_pair_kernel<T, TD, STAGES, EPI> (one CTA
+// per SM; a pair must sit in one GPC), asked of the occupancy calculator once per process.
+template <typename T, typename TD, int STAGES, int EPI>
+int pair_slots() {
+  static std::atomic<int> cached{0};
+  int v = cached.load();
+  if (v != 0) return v;
+  auto kernel = gemm_tc_pair_kernel<T, TD, STAGES, EPI>;
+  using S = PairSmem<STAGES>;
+  NTB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = S::TOTAL;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = 2;
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  NTB_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+  NTB_UNSUP(n > 0, "the device schedules no CTA pair of the GEMM kernel");
+  cached.store(n);
+  return n;
+}
+
+template <typename T, typename TD, int STAGES, int EPI = kEpiPlain>
+int launch_tc_pair(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& oa, const Operand& ob,
+                   CUtensorMapDataType tdt, cudaStream_t st) {
+  using S = PairSmem<STAGES>;
+  constexpr int BK = kRowBytes / 2;
+  const int es = 2;
+  CUtensorMap ta, tb;
+  int rc;
+  const uint64_t B = (uint64_t)p.batch;
+  // Each CTA loads 128 rows of A and 128 columns of B per stage.
+  if (!p.a_mn)
+    rc = tma::encode_3d(&ta, tdt, a->data, p.K, p.M, B, oa.s_outer * es, (B > 1 ? oa.bs : oa.s_outer * p.M) * es,
+                        BK, BM);
+  else
+    rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, B, oa.s_k * es, (B > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
+  if (rc != NTB_OK) return rc;
+  if (!p.b_mn)
+    rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, B, ob.s_outer * es, (B > 1 ? ob.bs : ob.s_outer * p.N) * es,
+                        BK, kPairBN / 2);
+  else
+    rc = tma::encode_3d(&tb, tdt, bm->data, p.N, p.K, B, ob.s_k * es, (B > 1 ? ob.bs : ob.s_k * p.K) * es, 64, BK);
+  if (rc != NTB_OK) return rc;
+  p.kblocks = (p.K + BK - 1) / BK;
+  p.mblocks = (p.M + kPairBM - 1) / kPairBM;
+  p.nblocks = (p.N + kPairBN - 1) / kPairBN;
+  p.tiles = p.mblocks * p.nblocks * p.batch;
+  {
+    // raster band of 256-row blocks whose A rows stay within ~48 MB of L2 (4..32 blocks)
+    const int64_t a_band_bytes = (int64_t)kPairBM * p.K * es;
+    int g = 32;
+    while (g > 4 && (int64_t)g * a_band_bytes > (48ll << 20)) g >>= 1;
+    p.band = g;
+  }
+  auto kernel = gemm_tc_pair_kernel<T, TD, STAGES, EPI>;
+  const int slots = pair_slots<T, TD, STAGES, EPI>();
+  if (slots < 0) return NTB_ERR_CUDA;
+  const int pairs = p.tiles < slots ? p.tiles : slots;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = S::TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = 2;
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  NTB_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tb, p));
+  NTB_LAUNCH_CHECK();
+  return NTB_OK;
+}
+
+// 16-bit GEMMs with at least two 128-row blocks run on CTA pairs.
+inline bool use_pair(const Params& p) {
+  return p.M > BM;
 }
 
 template <typename T>
@@ -664,6 +989,11 @@ extern "C" int ntb_gemm(const NtbTensor* a, const NtbTensor* bm, const NtbTensor
       const double e128 = 0.68 * (double)t128 / (std::ceil((double)t128 / sms) * sms);
       wide = e256 >= e128;
     }
+    if (wide && half_t && use_pair(p)) {
+      if (a->dtype == NTB_BF16)
+        return launch_tc_pair<__nv_bfloat16, __nv_bfloat16, 6>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
+      return launch_tc_pair<__half, __half, 6>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
+    }
     switch (a->dtype) {
       case NTB_BF16:
         return wide ? launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4>(a, bm, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st)
@@ -720,11 +1050,16 @@ extern "C" int ntb_gemm_swiglu(const NtbTensor* a, const NtbTensor* w, const Ntb
     NTB_UNSUP(tma_operand_ok<__nv_bfloat16>(a, oa, p.a_mn, p.M, p.K, 1) &&
                   tma_operand_ok<__nv_bfloat16>(w, ob, p.b_mn, p.N, p.K, 1),
               "operand rows are not 16-byte aligned for TMA");
+    if (use_pair(p))
+      return launch_tc_pair<__nv_bfloat16, __nv_bfloat16, 6, kEpiSwiGLU>(a, w, p, oa, ob,
+                                                                     CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
     return launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4, kEpiSwiGLU>(a, w, p, oa, ob,
                                                                         CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
   }
   NTB_UNSUP(tma_operand_ok<__half>(a, oa, p.a_mn, p.M, p.K, 1) && tma_operand_ok<__half>(w, ob, p.b_mn, p.N, p.K, 1),
             "operand rows are not 16-byte aligned for TMA");
+  if (use_pair(p))
+    return launch_tc_pair<__half, __half, 6, kEpiSwiGLU>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
   return launch_tc<__half, __half, 256, 4, kEpiSwiGLU>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
 }
 
@@ -786,10 +1121,15 @@ extern "C" int ntb_gemm_rope(const NtbTensor* a, const NtbTensor* w, const NtbTe
     NTB_UNSUP(tma_operand_ok<__nv_bfloat16>(a, oa, p.a_mn, p.M, p.K, 1) &&
                   tma_operand_ok<__nv_bfloat16>(w, ob, p.b_mn, p.N, p.K, 1),
               "operand rows are not 16-byte aligned for TMA");
+    if (use_pair(p))
+      return launch_tc_pair<__nv_bfloat16, __nv_bfloat16, 6, kEpiRope>(a, w, p, oa, ob,
+                                                                     CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
     return launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4, kEpiRope>(a, w, p, oa, ob,
                                                                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
   }
   NTB_UNSUP(tma_operand_ok<__half>(a, oa, p.a_mn, p.M, p.K, 1) && tma_operand_ok<__half>(w, ob, p.b_mn, p.N, p.K, 1),
             "operand rows are not 16-byte aligned for TMA");
+  if (use_pair(p))
+    return launch_tc_pair<__half, __half, 6, kEpiRope>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
   return launch_tc<__half, __half, 256, 4, kEpiRope>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
 }

@@ -46,7 +46,11 @@ def test_mm_random(mnk, dtype):
     _check(nt.mm(a.to(DEV), b.to(DEV)), O.mm(a, b), dtype, k)
 
 
-TC_SHAPES = [(128, 256, 64), (256, 512, 1024), (300, 712, 520), (1000, 136, 2056), (8, 8, 8), (129, 264, 72)]
+# 128-row problems run on single-SM tiles, larger ones on CTA pairs (256 x 256 tiles over two
+# SMs): edge tiles where the second CTA of a pair holds only padding rows (129, 300) or padding
+# columns (136), and a problem with more tiles than resident pairs (4096 x 2560).
+TC_SHAPES = [(128, 256, 64), (256, 512, 1024), (300, 712, 520), (1000, 136, 2056), (8, 8, 8), (129, 264, 72),
+             (4096, 2560, 512)]
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
@@ -63,7 +67,7 @@ def test_mm_tensor_core(shape, majors, dtype):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 def test_bmm(dtype):
-    for b_, m, n, k in [(3, 65, 130, 70), (2, 128, 256, 128), (4, 200, 48, 264)]:
+    for b_, m, n, k in [(3, 65, 130, 70), (2, 128, 256, 128), (4, 200, 48, 264), (2, 384, 520, 320)]:
         a, bb = _randn((b_, m, k), dtype), _randn((b_, k, n), dtype)
         _check(nt.bmm(a.to(DEV), bb.to(DEV)), O.bmm(a, bb), dtype, k)
 
