@@ -45,9 +45,9 @@ GLOBAL_BATCH = 16
 SEQ = 2048
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) of one launch of the fused gate/up (SwiGLU) projection at the full
-# chain size: ncu dram__bytes_read.sum 2.344712 GB + dram__bytes_write.sum 0.931517 GB
-# (profiles/gemm_tc_kernel-swiglu_32768x28672x4096_bf16.md).
-SWIGLU_GEMM_TRAFFIC = 3_276_228_928
+# chain size: ncu dram__bytes_read.sum 4.700038 GB + dram__bytes_write.sum 0.932619 GB
+# (profiles/gemm_tc_pair_kernel-swiglu_32768x28672x4096_bf16.md).
+SWIGLU_GEMM_TRAFFIC = 5_632_656_752
 
 
 def load_peaks():
@@ -586,7 +586,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": x.numel() * 2 * world,
                     "d2h_bytes_per_step": y.numel() * 2 * world},
             "gpu_launches": launches * world,
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (SwiGLU epilogue)",
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_pair_kernel (SwiGLU epilogue)",
                          "launch": f"fused gate/up projection [{gm}x{gk}]x[{gk}x{gn}] bf16 -> [{gm}x{gn // 2}] "
                                    "(largest of the 4 per step)",
                          "achieved": gate_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
@@ -595,7 +595,7 @@ def main():
                          "traffic_note": "measured at the full one-GPU size (16 x 2048 tokens)",
                          "traffic_algorithmic": (gm * gk + gk * gn + gm * gn // 2) * 2,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
-                                           "shape (profiles/gemm_tc_kernel-swiglu_32768x28672x4096_bf16.md)",
+                                           "shape (profiles/gemm_tc_pair_kernel-swiglu_32768x28672x4096_bf16.md)",
                          "peak_source": f"bf16_tflops_sustained, {peak_src}",
                          "all_gemms": {"achieved": gemm_tflops, "frac": gemm_tflops / peaks["bf16_tflops_sustained"],
                                        "share_of_step": gemm_ms / ms_local}},
