@@ -292,7 +292,9 @@ def per_op_table(dev, peaks):
     k = torch.randn(16, 2048, 8, 128, generator=g, device=dev).to(torch.bfloat16)
     sn, cs = rope_tables(2048, dev)
     bw("rope_bf16_q", lambda: nt.rotary_position_embedding(q, sn, cs, interleaved=False), 2 * q.numel() * 2)
-    bw("rope_bf16_k", lambda: nt.rotary_position_embedding(k, sn, cs, interleaved=False), 2 * k.numel() * 2)
+    # k is 64 MB (below L2): L2 is flushed between iterations
+    bw("rope_bf16_k", lambda: nt.rotary_position_embedding(k, sn, cs, interleaved=False), 2 * k.numel() * 2,
+       use_flush=True)
     del q, k
     # C5
     A = (torch.randn(16384, 8192, generator=g, device=dev)).to(torch.bfloat16)
