@@ -123,9 +123,21 @@ struct InPtrs {
   int scalar[NIN];  // 1 = stride 0 over the whole range (load element 0 once)
 };
 
+// Resident blocks per SM the flat kernel asks the compiler to allow for (a register cap): 1 for
+// streaming ops; arithmetic-heavy functors declare `static constexpr int kMinBlocks` so more
+// warps hide their math latency.
+template <typename Op, typename TI, typename = void>
+struct MinBlocks {
+  static constexpr int value = 1;
+};
+template <typename Op, typename TI>
+struct MinBlocks<Op, TI, std::void_t<decltype(Op::kMinBlocks)>> {
+  static constexpr int value = Op::kMinBlocks;
+};
+
 // Flat path: every input is unit-stride or a broadcast scalar; output unit-stride.
 template <int NIN, typename TI, typename TO, typename Op, int VEC>
-__global__ void __launch_bounds__(kThreads) flat_kernel(Op op, InPtrs<NIN> in, TO* __restrict__ out,
+__global__ void __launch_bounds__(kThreads, MinBlocks<Op, TI>::value) flat_kernel(Op op, InPtrs<NIN> in, TO* __restrict__ out,
                                                         int64_t n) {
   const TI* ip[NIN];
   TI sv[NIN];

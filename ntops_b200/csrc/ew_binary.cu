@@ -4,6 +4,12 @@
 #include "ew_ops.cuh"
 
 namespace ntb {
+namespace ew {
+// fp16 division runs an IEEE fp32 division per element (~100 registers with 8 elements per
+// vector, 2 blocks per SM); a cap at 3 blocks per SM keeps more warps in flight (0.92 -> 0.96 of
+// HBM).  The bf16 instantiation spills under the same cap and runs slower, so it keeps 2.
+template <> struct MinBlocks<ops::Div, __half, void> { static constexpr int value = 3; };
+}  // namespace ew
 namespace {
 
 template <typename Op>
