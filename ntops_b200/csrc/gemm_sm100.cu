@@ -758,12 +758,16 @@ int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& 
 }
 
 // Pairs of CTAs the device keeps resident for gemm_tc_pair_kernel<T, TD, STAGES, EPI> (one CTA
-// per SM; a pair must sit in one GPC), asked of the occupancy calculator once per process.
+// per SM; a pair must sit in one GPC), asked of the occupancy calculator once per process and
+// written to *slots; returns a status.
 template <typename T, typename TD, int STAGES, int EPI>
-int pair_slots() {
+int pair_slots(int* slots) {
   static std::atomic<int> cached{0};
-  int v = cached.load();
-  if (v != 0) return v;
+  const int v = cached.load();
+  if (v != 0) {
+    *slots = v;
+    return NTB_OK;
+  }
   auto kernel = gemm_tc_pair_kernel<T, TD, STAGES, EPI>;
   using S = PairSmem<STAGES>;
   NTB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
@@ -782,7 +786,8 @@ int pair_slots() {
   NTB_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
   NTB_UNSUP(n > 0, "the device schedules no CTA pair of the GEMM kernel");
   cached.store(n);
-  return n;
+  *slots = n;
+  return NTB_OK;
 }
 
 template <typename T, typename TD, int STAGES, int EPI = kEpiPlain>
@@ -819,8 +824,8 @@ int launch_tc_pair(const NtbTensor* a, const NtbTensor* bm, Params p, const Oper
     p.band = g;
   }
   auto kernel = gemm_tc_pair_kernel<T, TD, STAGES, EPI>;
-  const int slots = pair_slots<T, TD, STAGES, EPI>();
-  if (slots < 0) return NTB_ERR_CUDA;
+  int slots = 0;
+  if ((rc = pair_slots<T, TD, STAGES, EPI>(&slots)) != NTB_OK) return rc;
   const int pairs = p.tiles < slots ? p.tiles : slots;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
