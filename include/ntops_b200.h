@@ -273,8 +273,10 @@ NTB_API int ntb_sdpa_decode(const NtbTensor* q, const NtbTensor* k, const NtbTen
  * GPU that loads the library holds until exit, and are refused with NTB_ERR_UNSUPPORTED when
  * their partials need more.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
- * that device current; make that first call before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race.  Allocates nothing (no cudaMalloc / cudaFree).
+ * that device current; make that first call before any stream capture.  The address is kept
+ * for the life of the process, so do not call this after resetting the device.  All calls
+ * share the array: calls that overlap on the GPU race.  Allocates nothing (no cudaMalloc /
+ * cudaFree).
  * This entry point has no counterpart in the reference. */
 NTB_API int ntb_sdpa_decode_static(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v,
                                    const NtbTensor* mask, const NtbTensor* o, double scale, int causal_variant,

@@ -576,17 +576,22 @@ __global__ void __launch_bounds__(kThreads) decode_merge(Args a) {
 }
 
 // ---------------------------------------------------------------------------- host -------
-// How many clusters of c decode_mma<T, D> CTAs (c = 1..kMaxCluster) the device keeps resident
-// at once (0: not schedulable), asked of the occupancy calculator once per process.  A cluster
-// must fit inside one GPC, so this is not simply the resident CTAs per device / c.
+// How many clusters of c decode_mma<T, D> CTAs (c = 1..kMaxCluster) the current device keeps
+// resident at once (0: not schedulable), asked of the occupancy calculator once per device
+// (devices may differ in SM / GPC counts).  A cluster must fit inside one GPC, so this is not
+// simply the resident CTAs per device / c.  Returns nullptr for a device index beyond the cache.
 template <typename T, int D>
 const int* mma_cluster_occupancy() {
-  static std::atomic<int> ready{0};
-  static int occ[kMaxCluster + 1];
+  constexpr int kDevs = 64;
+  static std::atomic<int> ready[kDevs] = {};
+  static int occ_all[kDevs][kMaxCluster + 1];
   static std::mutex mu;
-  if (ready.load()) return occ;
+  const int dev = current_device();
+  if (dev < 0 || dev >= kDevs) return nullptr;
+  int* occ = occ_all[dev];
+  if (ready[dev].load()) return occ;
   std::lock_guard<std::mutex> lock(mu);
-  if (ready.load()) return occ;
+  if (ready[dev].load()) return occ;
   auto k = decode_mma<T, D>;
   occ[0] = 0;
   const bool attrs_ok =
@@ -609,7 +614,7 @@ const int* mma_cluster_occupancy() {
     occ[c] = n;
   }
   (void)cudaGetLastError();  // a refused query leaves no error behind
-  ready.store(1);
+  ready[dev].store(1);
   return occ;
 }
 
@@ -694,6 +699,7 @@ int plan(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTe
                          ? (a->D == 128 ? mma_cluster_occupancy<__nv_bfloat16, 128>()
                                         : mma_cluster_occupancy<__nv_bfloat16, 64>())
                          : (a->D == 128 ? mma_cluster_occupancy<__half, 128>() : mma_cluster_occupancy<__half, 64>());
+    NTB_ARG(occ != nullptr, "device index out of range");
     splits = 1;
     for (int c = std::min(kMaxCluster, std::max(max_splits, 1)); c >= 1; --c)
       if (occ[c] >= units) {
@@ -845,7 +851,9 @@ static __device__ __align__(256) float g_static_scratch[kStaticScratchBytes / si
 
 // Device address of g_static_scratch on the current device.  In host code the array's name only
 // stands in for the device copy, so the address is asked of the runtime once per device (with
-// that device current) and cached.
+// that device current) and cached for the life of the process.  The cache does not survive a
+// reset of the device (cudaDeviceReset, or the primary context released and created again): a
+// process that resets a device must not call ntb_sdpa_decode_static on it afterwards.
 int static_scratch(float** out) {
   static std::mutex mu;
   static float* cache[64] = {nullptr};

@@ -31,7 +31,7 @@
 #include "tma.cuh"
 
 namespace ntb {
-namespace fmha {
+namespace attn {
 
 constexpr int BLK = 128;         // query rows per Q tile and keys per KV block
 constexpr int kTiles = 2;        // Q tiles per CTA (ping-pong between two softmax warpgroups)
@@ -109,7 +109,7 @@ constexpr uint32_t kOCol = 256;
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
-    fmha_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, Params p) {
   using S = Smem<D>;
   constexpr uint32_t kFormat = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
@@ -418,7 +418,7 @@ constexpr int kGenRows = 4;
 constexpr int kGenKeys = 32;
 
 template <typename T, typename Acc>
-__global__ void __launch_bounds__(128) fmha_generic_kernel(GenArgs a, Params p) {
+__global__ void __launch_bounds__(128) attn_generic_kernel(GenArgs a, Params p) {
   extern __shared__ __align__(16) uint8_t gsm[];
   const int D = p.D, Dv = a.Dv;
   Acc* Ks = reinterpret_cast<Acc*>(gsm);                  // [kGenKeys][D + 1]
@@ -526,7 +526,7 @@ int launch_tc(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, Params
   if ((rc = tma::encode_4d(&tv, tdt, v->data, p.D, p.Skv, p.Hkv, p.B, sb(v, 2), sb(v, 1), sb(v, 0), 64, BLK)) !=
       NTB_OK)
     return rc;
-  auto kernel = fmha_tc_kernel<T, D>;
+  auto kernel = attn_tc_kernel<T, D>;
   {
     // The register split assumes the compiled launch register count (kLaunchRegs).
     static std::atomic<int> regs_ok{0};
@@ -570,7 +570,7 @@ int launch_generic(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, c
   a.Dv = Dv;
   const size_t smem = sizeof(Acc) * ((size_t)kGenKeys * (p.D + 1) + (size_t)kGenKeys * (Dv + 1) +
                                      (size_t)kGenRows * p.D + (size_t)kGenRows * kGenKeys);
-  auto kernel = fmha_generic_kernel<T, Acc>;
+  auto kernel = attn_generic_kernel<T, Acc>;
   if (smem > 48 * 1024) NTB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t grid = (int64_t)p.B * p.Hq * ((p.Sq + kGenRows - 1) / kGenRows);
   NTB_UNSUP(grid <= 0x7fffffffLL, "attention grid too large");
@@ -587,13 +587,13 @@ bool tma_attn_ok(const NtbTensor* t, int es) {
   return true;
 }
 
-}  // namespace fmha
+}  // namespace attn
 }  // namespace ntb
 
 extern "C" int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
                         const NtbTensor* o, double scale, int causal_variant, void* stream) {
   using namespace ntb;
-  using namespace ntb::fmha;
+  using namespace ntb::attn;
   int rc;
   if ((rc = check_tensor(q, "query")) != NTB_OK) return rc;
   if ((rc = check_tensor(k, "key")) != NTB_OK) return rc;

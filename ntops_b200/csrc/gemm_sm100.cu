@@ -757,13 +757,15 @@ int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& 
   return NTB_OK;
 }
 
-// Pairs of CTAs the device keeps resident for gemm_tc_pair_kernel<T, TD, STAGES, EPI> (one CTA
-// per SM; a pair must sit in one GPC), asked of the occupancy calculator once per process and
-// written to *slots; returns a status.
+// Pairs of CTAs the current device keeps resident for gemm_tc_pair_kernel<T, TD, STAGES, EPI>
+// (one CTA per SM; a pair must sit in one GPC), asked of the occupancy calculator once per device
+// (devices may differ in SM / GPC counts) and written to *slots; returns a status.
 template <typename T, typename TD, int STAGES, int EPI>
 int pair_slots(int* slots) {
-  static std::atomic<int> cached{0};
-  const int v = cached.load();
+  static std::atomic<int> cached[64] = {};
+  const int dev = current_device();
+  NTB_ARG(dev >= 0 && dev < 64, "device index %d out of range", dev);
+  const int v = cached[dev].load();
   if (v != 0) {
     *slots = v;
     return NTB_OK;
@@ -785,7 +787,7 @@ int pair_slots(int* slots) {
   int n = 0;
   NTB_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
   NTB_UNSUP(n > 0, "the device schedules no CTA pair of the GEMM kernel");
-  cached.store(n);
+  cached[dev].store(n);
   *slots = n;
   return NTB_OK;
 }

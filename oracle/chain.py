@@ -8,6 +8,25 @@ import torch
 from oracle import ops as O
 
 HIDDEN, HEADS, KV_HEADS, HEAD_DIM, FFN, EPS = 4096, 32, 8, 128, 14336, 1e-5
+THETA = 500000.0  # RoPE base of Llama-3-8B
+
+
+def rope_tables(seq_len, dtype=torch.bfloat16):
+    """sin / cos tables [S, D/2] for positions 0..S-1 on the CPU (the reference RoPE test's
+    recipe, tests/test_rotary_position_embedding.py:32-45, with base THETA)."""
+    return O.rope_tables(seq_len, HEAD_DIM, base=THETA, dtype=dtype)
+
+
+def random_weights(generator, dtype=torch.bfloat16):
+    """Random-init weights ~N(0, 0.02) in [in, out] layout on the CPU, in the order
+    layer_forward takes them (wq, wk, wv, wo, wg, wu, wd, norm1, norm2); norm weights ones."""
+
+    def w(k, n):
+        return (torch.randn((k, n), generator=generator) * 0.02).to(dtype)
+
+    return [w(HIDDEN, HEADS * HEAD_DIM), w(HIDDEN, KV_HEADS * HEAD_DIM), w(HIDDEN, KV_HEADS * HEAD_DIM),
+            w(HEADS * HEAD_DIM, HIDDEN), w(HIDDEN, FFN), w(HIDDEN, FFN), w(FFN, HIDDEN),
+            torch.ones(HIDDEN, dtype=dtype), torch.ones(HIDDEN, dtype=dtype)]
 
 
 def layer_forward(x, w, sin, cos):

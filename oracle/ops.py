@@ -55,15 +55,36 @@ def mul(input, other):
     return a * b
 
 
+def _floor_divide_float(a, b):
+    """Floor division of floating-point a / b in a's dtype, the algorithm of CPython's
+    float_divmod (Objects/floatobject.c), which torch's div(rounding_mode="floor") follows:
+    remainder by fmod, quotient (a - mod) / b moved down by one when the remainder's sign differs
+    from the divisor's, then rounded to the nearest integer from below; b = 0 gives a / b."""
+    mod = torch.fmod(a, b)
+    div = (a - mod) / b
+    div = torch.where((mod != 0) & ((b < 0) != (mod < 0)), div - 1, div)
+    fd = torch.floor(div)
+    fd = torch.where(div - fd > 0.5, fd + 1, fd)
+    fd = torch.where(div == 0, torch.copysign(torch.zeros_like(div), a / b), fd)
+    return torch.where(b == 0, a / b, fd)
+
+
 def div(input, other, rounding_mode=None):
-    """kernels/div.py:9-18: true, trunc (cast of the quotient to int64) or floor division."""
+    """kernels/div.py:9-18: true, trunc (cast of the quotient to int64) or floor division.
+
+    True division runs in float64, rounded once.  The rounding modes give integer-valued
+    results that a float64 quotient could place on the other side of an integer, so they restate
+    the exact arithmetic instead: the quotient in the compute dtype (float32 for 16-bit and
+    float32 inputs, float64 for float64), then trunc, or the floor-division algorithm above;
+    the integer-valued result is rounded once to the input dtype."""
     a, b, dt = _promote(input, other)
     if rounding_mode is None:
         out_dt = dt if dt.is_floating_point else torch.get_default_dtype()
         return (_f(a) / _f(b)).to(out_dt)
     if dt.is_floating_point:
-        q = _f(a) / _f(b)
-        q = torch.trunc(q) if rounding_mode == "trunc" else torch.floor(q)
+        ct = F64 if dt == F64 else torch.float32
+        ac, bc = a.to(ct), b.to(ct)
+        q = torch.trunc(ac / bc) if rounding_mode == "trunc" else _floor_divide_float(ac, bc)
         return q.to(dt)
     if rounding_mode == "trunc":
         return torch.div(a, b, rounding_mode="trunc")

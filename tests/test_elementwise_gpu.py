@@ -89,9 +89,27 @@ def test_div(rounding_mode, case):
     if rounding_mode is None:
         assert_close(got, want)
     else:
-        # Integer-valued results: equal except where a/b lies within rounding of an integer.
-        diff = (got.cpu().double() - want.double()).abs()
-        assert (diff > 0).float().mean() < 0.01
+        # integer-valued results: bit-exact against the oracle's exact restatement
+        torch.testing.assert_close(got.cpu(), want, rtol=0, atol=0, equal_nan=True)
+
+
+@pytest.mark.parametrize("rounding_mode", ["trunc", "floor"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16, torch.float64])
+def test_div_rounding_edges(rounding_mode, dtype):
+    # quotients at and next to integers, signed zeros, mixed signs, zero / inf / nan divisors
+    g = torch.Generator().manual_seed(17)
+    q = torch.randint(-50, 50, (4000,), generator=g).to(torch.float64)
+    b = (torch.rand(4000, generator=g, dtype=torch.float64) * 8 - 4)
+    a = q * b
+    a[::3] = torch.nextafter(a[::3], torch.full_like(a[::3], float("inf")))
+    a[1::3] = torch.nextafter(a[1::3], torch.full_like(a[1::3], float("-inf")))
+    special = torch.tensor([0.0, -0.0, 1.0, -1.0, 7.0, -7.0, float("inf"), float("-inf"), float("nan")],
+                           dtype=torch.float64)
+    a = torch.cat((a, special.repeat_interleave(len(special))))
+    b = torch.cat((b, special.repeat(len(special))))
+    a, b = a.to(dtype), b.to(dtype)
+    got = nt.div(a.to(DEV), b.to(DEV), rounding_mode=rounding_mode).cpu()
+    torch.testing.assert_close(got, O.div(a, b, rounding_mode), rtol=0, atol=0, equal_nan=True)
 
 
 @pytest.mark.parametrize("case", FLOAT_CASES, ids=case_id)
