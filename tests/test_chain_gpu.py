@@ -66,13 +66,17 @@ def test_layer_chain_small(fused):
     got = chain.layer_forward(x.to(DEV), wts, sin, cos, fused=fused).cpu()
     w_cpu = [t.cpu() for t in (wts.wq, wts.wk, wts.wv, wts.wo, wts.wg, wts.wu, wts.wd, wts.norm1, wts.norm2)]
     want = OC.layer_forward(x, w_cpu, sin.cpu(), cos.cpu())
-    # bf16 intermediates are rounded at different points on the two sides, so every element is
-    # held to |got - want| <= 1e-2 |want| + 3e-2 rms(want): the bound PyTorch's own bf16 CPU
-    # chain (oracle/chain.py:layer_forward_torch_cpu) meets against the same fp64 oracle.
+    # bf16 intermediates are rounded at different points on the two sides.  Every element is held
+    # to |got - want| <= 1e-2 |want| + 5e-2 rms(want) (single-element outliers of PyTorch's own
+    # bf16 CPU chain, oracle/chain.py:layer_forward_torch_cpu, reach ~0.04 rms against the same
+    # fp64 oracle), the mean error to 1e-2 rms, and the mean error may not exceed 1.25 times that
+    # of PyTorch's bf16 chain on the same inputs.
     w64 = want.double()
     rms = w64.pow(2).mean().sqrt().item()
     err = (got.double() - w64).abs()
-    bad = int((err > 1e-2 * w64.abs() + 3e-2 * rms).sum())
+    bad = int((err > 1e-2 * w64.abs() + 5e-2 * rms).sum())
     assert bad == 0, (bad, err.max().item() / rms)
     assert err.mean().item() < 1e-2 * rms, (err.mean().item(), rms)
+    torch_err = (OC.layer_forward_torch_cpu(x, w_cpu, sin.cpu(), cos.cpu()).double() - w64).abs().mean().item()
+    assert err.mean().item() <= 1.25 * torch_err, (err.mean().item(), torch_err)
     assert torch.isfinite(got.float()).all()
