@@ -125,14 +125,16 @@ struct InPtrs {
 
 // Resident blocks per SM the flat kernel asks the compiler to allow for (a register cap): 1 for
 // streaming ops; arithmetic-heavy functors declare `static constexpr int kMinBlocks` so more
-// warps hide their math latency.
+// warps (and more loads in flight) hide their math latency.  The cap applies to floating-point
+// element types only: integer instantiations of the same functors (integer division on 16-wide
+// byte vectors) would spill under it.
 template <typename Op, typename TI, typename = void>
 struct MinBlocks {
   static constexpr int value = 1;
 };
 template <typename Op, typename TI>
 struct MinBlocks<Op, TI, std::void_t<decltype(Op::kMinBlocks)>> {
-  static constexpr int value = Op::kMinBlocks;
+  static constexpr int value = std::is_integral<TI>::value ? 1 : Op::kMinBlocks;
 };
 
 // Flat path: every input is unit-stride or a broadcast scalar; output unit-stride.

@@ -71,6 +71,7 @@ struct Gelu {
   }
 };
 struct GeluTanh {
+  static constexpr int kMinBlocks = 3;  // 3 blocks per SM (fp32 outputs use this functor)
   template <typename T> __device__ T operator()(T x) const {
     const T kBeta = T(0.79788456080286535588);  // sqrt(2/pi)
     const T kKappa = T(0.044715);
@@ -148,7 +149,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 struct ExpFast { __device__ float operator()(float x) const { return hw_ex2(x * kLog2e); } };
 struct SigmoidFast { __device__ float operator()(float x) const { return hw_rcp(1.f + hw_ex2(-x * kLog2e)); } };
-struct SiluFast { __device__ float operator()(float x) const { return x * hw_rcp(1.f + hw_ex2(-x * kLog2e)); } };
+// capped at 80 registers (3 blocks per SM): x stays live across the unrolled vectors, and 2
+// blocks per SM keep too few loads in flight for a one-input stream
+struct SiluFast {
+  static constexpr int kMinBlocks = 3;
+  __device__ float operator()(float x) const { return x * hw_rcp(1.f + hw_ex2(-x * kLog2e)); }
+};
 struct GeluTanhFast {
   __device__ float operator()(float x) const {
     const float inner = 0.79788456080286535588f * (x + 0.044715f * x * x * x);
