@@ -7,20 +7,31 @@
 // acc / l.  The reference does not skip KV blocks above the causal diagonal.
 //
 // sm_100a kernel (bf16 / fp16, head_dim 64 or 128, no additive mask):
-//   * one CTA per (batch, q-head, 128-row Q tile), head-major so a head's K / V stay in L2;
-//     heavy causal tiles of a head are launched first;
-//   * warp 4 loads Q once and streams K / V blocks of 128 keys through a 2-deep TMA ring;
-//   * warp 5 owns TMEM (O: D columns, three S buffers of 128 columns) and issues
-//       S_j = Q K_j^T            (A = Q, B = K, both K-major, from shared memory)
-//       O  += P_j V_j            (A = P from TMEM, B = V MN-major from shared memory)
-//     in the order S_0, S_1, PV_0, S_2, PV_1, ... so the tensor core computes S_{j+1} while the
-//     softmax warps work on S_j;
-//   * warps 0-3 (one thread per query row) read S_j from TMEM, mask the diagonal / tail
-//     blocks, track the running max in base-2 units, write P_j = exp2(S*scale*log2e - m) as
-//     bf16/fp16 pairs over S_j's first 64 TMEM columns, and accumulate the row sum.  The O
-//     accumulator is rescaled only when a row's max grows by more than 8 (2^8 headroom), so
-//     O and l always share one reference max and O / l is exact;
+//   * one CTA per (batch, q-head, two Q tiles of 128 rows), head-major so a head's K / V stay
+//     in L2; heavy causal tiles of a head are launched first;
+//   * warp 1 loads both Q tiles once and streams K / V blocks of 128 keys through a 2-deep TMA
+//     ring;
+//   * warp 0 owns TMEM (per tile t: S_t, 128 columns, and O_t, D columns) and issues
+//       S_t(j) = Q_t K_j^T       (A = Q, B = K, both K-major, from shared memory)
+//       O_t   += P_t(j) V_j      (A = P from TMEM, B = V MN-major from shared memory)
+//     in the order S_0(0), S_1(0), then per block PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), so the
+//     tensor core works on one tile while the other tile's softmax runs.  The MMA and TMA warps
+//     are the lowest-numbered warps, and an MMA issue is one add to a prebuilt descriptor half
+//     plus the instruction: the issuing thread shares its sub-partition with softmax warps;
+//   * warps 4-7 and 8-11 (one thread per query row of tile 0 / 1) read S_t(j) from TMEM, mask
+//     the diagonal / tail blocks, track the running max in base-2 units, write P_t(j) =
+//     exp2(S * scale * log2e - m) as bf16 / fp16 pairs over S_t(j)'s first 64 TMEM columns,
+//     publish it, then sum the row.  The O accumulator is rescaled only when a row's max grows
+//     by more than 8 (2^8 headroom), so O and l always share one reference max and O / l is
+//     exact;
 //   * causal KV blocks wholly above the diagonal are skipped.
+// What bounds it (measured with cycle stamps on B200): a tile's softmax of a 128 x 128 score
+// block takes ~1750 cycles (1024 of them the 16384 exponentials on the 16-per-clock MUFU unit),
+// longer than the other tile's PV + S (16 MMAs, 1024 cycles at full rate), so the tensor pipe
+// drains once per block and restarts cold (a drained pipe runs the next 8 MMAs at ~110 cycles
+// each, against 64 when queued back to back).  Splitting a row's 128 columns over two threads
+// (both land on the same sub-partition) and moving 25-50 % of the exponentials to the FMA pipe
+// (exp2_poly2) were measured and did not shorten the per-tile chain.
 // fp32 / fp64 operands, additive masks, other head sizes and layouts TMA cannot address run
 // on the CUDA-core kernel at the end of this file (fp32 accumulation, fp64 for fp64).
 #include <atomic>
@@ -35,9 +46,12 @@ namespace attn {
 
 constexpr int BLK = 128;         // query rows per Q tile and keys per KV block
 constexpr int kTiles = 2;        // Q tiles per CTA (ping-pong between two softmax warpgroups)
-constexpr int kThreads = 384;    // warps 0-3 softmax tile 0, 4-7 softmax tile 1, 8 TMA, 9 MMA, 10-11 idle
-// Register split (setmaxnreg): the launch gives every thread kLaunchRegs; the TMA / MMA
-// warpgroup (warps 8-11) drops to kProdRegs and the two softmax warpgroups rise to kSoftRegs.
+constexpr int kThreads = 384;    // warp 0 MMA, 1 TMA, 2-3 idle, 4-7 softmax tile 0, 8-11 softmax tile 1
+constexpr int kSoftBase = 4;     // first softmax warp
+constexpr int kMmaWarp = 0;
+constexpr int kTmaWarp = 1;
+// Register split (setmaxnreg): the launch gives every thread kLaunchRegs; the MMA / TMA
+// warpgroup (warps 0-3) drops to kProdRegs and the two softmax warpgroups rise to kSoftRegs.
 // 8 * 32 * kSoftRegs + 4 * 32 * kProdRegs must not exceed kThreads * kLaunchRegs, or the raise
 // would wait forever; the host checks the compiled register count before launching.
 constexpr int kLaunchRegs = 168;
@@ -103,6 +117,43 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return r;
 }
 
+// max(a, b) that returns NaN when either input is NaN (max.NaN.f32).
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// 2^x for a pair of arguments on the FMA pipe, so that part of a score tile's exponentials
+// leave the MUFU unit (which alone would take as long as the tile's two MMAs).  Range
+// reduction in the style of Cody and Waite: adding 1.5 * 2^23 rounds x to the nearest integer n,
+// held in the low mantissa bits of t, and f = x - n lies in [-0.5, 0.5]; 2^f is a degree-3
+// polynomial whose coefficients are the minimax (Remez exchange) fit of 2^f on [-0.5, 0.5] in
+// relative error, max 7.5e-5 (fitted for this kernel; the probabilities are rounded to bf16 /
+// fp16 next, 2^-9 / 2^-11); n is added to the exponent field as an integer (t's bits shifted by
+// 23 carry exactly n there).  Arguments are clamped at -125 so 2^n stays a normal number (the
+// hardware path flushes the same range to zero; both are below any rounded probability); a NaN
+// argument stays NaN (max.NaN), +inf only arises from inf scores, whose row is NaN either way.
+// The largest argument here is the rescale threshold (x <= 8).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = max_nan(x.x, -125.f);
+  x.y = max_nan(x.y, -125.f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 q = __ffma2_rn(f, make_float2(0.0551716685f, 0.0551716685f), make_float2(0.2426111251f, 0.2426111251f));
+  q = __ffma2_rn(q, f, make_float2(0.6932609677f, 0.6932609677f));
+  q = __ffma2_rn(q, f, make_float2(0.9999280572f, 0.9999280572f));
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
+// Column pairs (of the 16 per 32-column chunk) whose exponentials take exp2_poly2.  Shares of
+// 4, 6 and 8 of 16 pairs were measured slower than none on B200 (the extra issue slots outweigh
+// the MUFU time saved while the per-tile chain above bounds the kernel), so none is used.
+constexpr uint32_t kPolyPairs = 0u;
+
 // TMEM columns: S_t at 128 t (P_t written over its first 64 columns), O_t at 256 + 128 t.
 constexpr uint32_t kSCol = 0;
 constexpr uint32_t kOCol = 256;
@@ -162,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     sm100::fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     sm100::tmem_alloc(tmem_slot, TMEM_COLS);
     sm100::tmem_relinquish();
   }
@@ -171,10 +222,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 8) {
-    // TMA / MMA warpgroup: few registers (all four warps execute the split together)
+  if (warp < kSoftBase) {
+    // MMA / TMA warpgroup: few registers (all four warps execute the split together)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs));
-  if (warp == 8) {
+  if (warp == kTmaWarp) {
     // ------------------------------------------------------------------ TMA producer ----
     if (lane == 0 && nkv > 0) {
       uint32_t armed_k = 0, armed_v = 0, par_k = 0, par_v = 0;
@@ -209,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (armed_v & (1u << st)) sm100::mbar_wait_unwind(&v_full[st], (par_v >> st) & 1u);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------- MMA issuer ----
     // Order: S_0(0), S_1(0), then per block j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1).  While one
     // softmax warpgroup works on its tile the tensor core runs the other tile's PV and next S.
@@ -219,7 +270,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t idesc_pv = sm100::instr_desc(kFormat, false, true, BLK, D);
     bool ok = nkv > 0 && sm100::mbar_wait(q_full, 0, abort_flag, p.err);
     sm100::tc_fence_after();
-    const uint32_t q_addr = sm100::smem_u32(sQ);
+    // Descriptor halves built once: an issue is then an add of a compile-time offset to a low
+    // half plus the MMA instruction, so the issuing thread keeps up with the tensor core while
+    // it shares its sub-partition's issue slots with four softmax warps.
+    const uint32_t d_hi = sm100::smem_desc_hi(1024);
+    uint32_t q_lo[kTiles], k_lo[2], v_lo[2];
+#pragma unroll
+    for (int t = 0; t < kTiles; ++t) q_lo[t] = sm100::smem_desc_lo(sm100::smem_u32(sQ + t * S::TILE), 16);
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+      k_lo[st] = sm100::smem_desc_lo(sm100::smem_u32(sK + st * S::TILE), 16);
+      v_lo[st] = sm100::smem_desc_lo(sm100::smem_u32(sV + st * S::TILE), S::SUB);
+    }
     // S_t(j) = Q_t K_j^T; the last tile to use K_j releases its stage.
     auto issue_s = [&](int t, int j, bool release_k) -> bool {
       const int st = j & 1;
@@ -228,14 +290,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tc_fence_after();
       }
       if (lane == 0) {
-        const uint32_t k_addr = sm100::smem_u32(sK + st * S::TILE);
-        const uint32_t qt_addr = q_addr + t * S::TILE;
+        const uint32_t a0 = q_lo[t], b0 = k_lo[st];
         const uint32_t d_tmem = tmem + kSCol + 128u * t;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * S::SUB + (kk & 3) * 32;
-          sm100::mma_f16(d_tmem, sm100::smem_desc(qt_addr + off, 16, 1024),
-                         sm100::smem_desc(k_addr + off, 16, 1024), idesc_qk, kk != 0);
+          const uint32_t off = ((kk >> 2) * S::SUB + (kk & 3) * 32) >> 4;
+          if (kk == 0)
+            sm100::mma_f16_lohi<false>(d_tmem, a0 + off, d_hi, b0 + off, d_hi, idesc_qk);
+          else
+            sm100::mma_f16_lohi<true>(d_tmem, a0 + off, d_hi, b0 + off, d_hi, idesc_qk);
         }
         sm100::mma_commit(&s_full[t]);
         if (release_k) sm100::mma_commit(&k_empty[st]);
@@ -250,13 +313,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (first_v && !sm100::mbar_wait(&v_full[st], (uint32_t)((j >> 1) & 1), abort_flag, p.err)) return false;
       sm100::tc_fence_after();
       if (lane == 0) {
-        const uint32_t v_addr = sm100::smem_u32(sV + st * S::TILE);
+        const uint32_t b0 = v_lo[st];
         const uint32_t p_tmem = tmem + kSCol + 128u * t;
         const uint32_t o_tmem = tmem + kOCol + 128u * t;
 #pragma unroll
-        for (int kk = 0; kk < BLK / 16; ++kk)
-          sm100::mma_f16_ts(o_tmem, p_tmem + kk * 8, sm100::smem_desc(v_addr + kk * 16 * 128, S::SUB, 1024),
-                            idesc_pv, (j | kk) != 0);
+        for (int kk = 0; kk < BLK / 16; ++kk) {
+          const uint32_t off = (kk * 16 * 128) >> 4;
+          if (kk == 0 && j == 0)
+            sm100::mma_f16_ts_lohi<false>(o_tmem, p_tmem + kk * 8, b0 + off, d_hi, idesc_pv);
+          else
+            sm100::mma_f16_ts_lohi<true>(o_tmem, p_tmem + kk * 8, b0 + off, d_hi, idesc_pv);
+        }
         sm100::mma_commit(&pv_done[t]);
         if (release_v) sm100::mma_commit(&v_empty[st]);
       }
@@ -283,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------- softmax warpgroups ----
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftRegs));
-    const int t = warp >> 2;                       // Q tile of this warpgroup
+    const int t = (warp - kSoftBase) >> 2;         // Q tile of this warpgroup
     const int wq = warp & 3;                       // TMEM lane quarter
     const int row = q0 + t * BLK + wq * 32 + lane; // query row of this thread
     const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
@@ -312,14 +379,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (k0 + c * 32 + i > kmax) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      // row max: three-input max over pairs, 4 independent chains
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // row max: eight independent chains of three-input maxima (16 columns each)
+      float mx8[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t* v = &sr[k >> 1][(k & 1) * 16];
+        float m = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          mx4[i & 3] = max3f(mx4[i & 3], __uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1]));
-      const float mx = max3f(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
+        for (int i = 3; i + 1 < 16; i += 2) m = max3f(m, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+        mx8[k] = fmaxf(m, __uint_as_float(v[15]));
+      }
+      const float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
       const float m_blk = mx * p.scale_log2;
       // Rescale O and l only when the max grows by more than the threshold (done after P is
       // written, before P is published: PV_t(j) must accumulate into the rescaled O).
@@ -327,26 +397,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_prev = m_used;
       if (grow) m_used = m_blk;
       const float m_ref = m_used == -INFINITY ? 0.f : m_used;
-      // P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns; the
-      // argument and the row sum use the packed fp32x2 instructions
+      // P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns, the
+      // argument in packed fp32x2; the fp32 probabilities stay in sr for the row sum, which is
+      // taken after P is published (off the path to the next MMA)
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_ref, -m_ref);
-      float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])), sc2, nm2);
-          x.x = sm100::ex2_approx(x.x);
-          x.y = sm100::ex2_approx(x.y);
-          sum2[i & 1] = __fadd2_rn(sum2[i & 1], x);
+          if ((kPolyPairs >> i) & 1u) {
+            x = exp2_poly2(x);
+          } else {
+            x.x = sm100::ex2_approx(x.x);
+            x.y = sm100::ex2_approx(x.y);
+          }
+          sr[c][2 * i] = __float_as_uint(x.x);
+          sr[c][2 * i + 1] = __float_as_uint(x.y);
           pk[i] = pack2<T>(x.x, x.y);
         }
         sm100::tmem_st_32x32b_x16(s_tmem + c * 16, pk);
       }
-      const float2 sum = __fadd2_rn(sum2[0], sum2[1]);
+      float alpha = 1.f;
       if (__any_sync(0xffffffffu, grow && j > 0)) {
-        const float alpha = grow ? exp2f(m_prev - m_blk) : 1.f;
+        alpha = grow ? exp2f(m_prev - m_blk) : 1.f;
         // PV_t(j-1) (and, by commit order, every earlier PV of this tile) must be complete.
         if (!sm100::mbar_wait(&pv_done[t], (uint32_t)((j - 1) & 1), abort_flag, p.err)) { ok = false; break; }
         sm100::tc_fence_after();
@@ -359,12 +434,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
           sm100::tmem_st_32x32b_x32(o_tmem + c * 32, r);
         }
-        l *= alpha;
       }
-      l += sum.x + sum.y;
       sm100::tmem_st_wait();
       sm100::tc_fence_before();
       sm100::mbar_arrive(&p_full[t]);
+      // row sum of the fp32 probabilities: packed adds over 8 independent partial sums
+      float2 sum8[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          sum8[i & 3] = __fadd2_rn(sum8[i & 3], make_float2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])));
+      const float2 sum = __fadd2_rn(__fadd2_rn(sum8[0], sum8[1]), __fadd2_rn(sum8[2], sum8[3]));
+      l = l * alpha + (sum.x + sum.y);
     }
     // Epilogue: O / l, written as this row's D contiguous elements.
     if (ok && nkv_mine > 0)
@@ -397,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, TMEM_COLS);
   }

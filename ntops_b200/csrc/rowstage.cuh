@@ -137,9 +137,9 @@ struct Ring {
   __device__ __forceinline__ const T* wait(bool& fail) {
     const int s = cslot;
     const uint32_t par = (phases >> s) & 1u;
-    if (!sm100::mbar_try_wait(&bar[s], par)) {
+    if (!sm100::mbar_try_wait_default(&bar[s], par)) {
       const uint64_t t0 = sm100::globaltimer();
-      while (!sm100::mbar_try_wait(&bar[s], par)) {
+      while (!sm100::mbar_try_wait_default(&bar[s], par)) {
         if (sm100::globaltimer() - t0 > sm100::kWaitTimeoutNs) {
           fail = true;
           break;
