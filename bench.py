@@ -397,6 +397,20 @@ def per_op_table(dev, peaks, with_cpu=True):
        fl * (8192 + 1) / (2 * 8192),
        cpu=(lambda: F.scaled_dot_product_attention(qac, kac, vac, is_causal=True), note, 256.0))
     del qa, ka, va, qac, kac, vac
+    # conv2d (§8 f3; not a BASELINE config): a ResNet-style 3x3 layer, bf16, N32 C256 56x56 ->
+    # K256, pad 1 (the CPU leg times one image and scales by 32)
+    xc = torch.randn(32, 256, 56, 56, generator=g, device=dev).to(torch.bfloat16)
+    wc = (torch.randn(256, 256, 3, 3, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    xcc, wcc = (xc[:1].cpu(), wc.cpu()) if with_cpu else (None, None)
+    tf("conv2d_bf16_n32_c256_56x56_k256_3x3", lambda: nt.conv2d(xc, wc, None, 1, 1), 2 * 32 * 256 * 256 * 9 * 56 * 56,
+       cpu=(lambda: F.conv2d(xcc, wcc, None, 1, 1), "1 of 32 images, time x 32", 32.0))
+    del xc, wc, xcc
+    # dropout (§8 f3): p = 0.1 over 2^28 bf16 elements, HBM-bound (one read, one write)
+    xdp = torch.randn(n, generator=g, device=dev).to(torch.bfloat16)
+    xdpc = xdp.cpu() if with_cpu else None
+    bw("dropout_bf16_p0.1", lambda: nt.dropout(xdp, 0.1), 2 * n * 2,
+       cpu=(lambda: F.dropout(xdpc, 0.1, training=True),))
+    del xdp, xdpc
     # decode step against an 8192-token KV cache (Llama-3-8B heads): HBM-bound on K / V
     qd = torch.randn(8, 32, 1, 128, generator=g, device=dev).to(torch.bfloat16)
     kd = torch.randn(8, 8, 8192, 128, generator=g, device=dev).to(torch.bfloat16)

@@ -70,6 +70,11 @@ struct Params {
   void* o;
   int64_t o_b, o_h, o_s;  // output strides (unit inner stride)
   unsigned int* err;
+  // additive mask [B, Hq, Sq, Skv] in the query's dtype (tc kernel: unit key stride), natural-log
+  // units; mask_vec: every row segment of 8 keys starting at a multiple of 8 is 16-byte aligned
+  const void* mask;
+  int64_t m_b, m_h, m_q;
+  int mask_vec;
 };
 
 template <int D>
@@ -158,7 +163,43 @@ constexpr uint32_t kPolyPairs = 0u;
 constexpr uint32_t kSCol = 0;
 constexpr uint32_t kOCol = 256;
 
-template <typename T, int D>
+// 16-bit value (bits) widened to fp32.
+template <typename T>
+__device__ __forceinline__ float widen16(uint32_t bits);
+template <>
+__device__ __forceinline__ float widen16<__nv_bfloat16>(uint32_t bits) {
+  return __uint_as_float(bits << 16);
+}
+template <>
+__device__ __forceinline__ float widen16<__half>(uint32_t bits) {
+  return __half2float(__ushort_as_half((unsigned short)bits));
+}
+
+// The 128 mask values of keys [k0, k0 + 128) of one row, as 16-bit values packed in pairs;
+// keys at or past Skv read as 0 (those keys are masked to -inf separately).
+template <typename T>
+__device__ __forceinline__ void load_mask_row(const T* mrow, int k0, int skv, bool vec, uint32_t (&mk)[64]) {
+  if (vec && k0 + BLK <= skv) {
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(mrow + k0 + 8 * g));
+      mk[4 * g] = v.x;
+      mk[4 * g + 1] = v.y;
+      mk[4 * g + 2] = v.z;
+      mk[4 * g + 3] = v.w;
+    }
+  } else {
+    const unsigned short* m16 = reinterpret_cast<const unsigned short*>(mrow);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const int k = k0 + 2 * i;
+      const uint32_t lo = k < skv ? m16[k] : 0u, hi = k + 1 < skv ? m16[k + 1] : 0u;
+      mk[i] = lo | (hi << 16);
+    }
+  }
+}
+
+template <typename T, int D, bool MASK>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, Params p) {
@@ -362,16 +403,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_used = -INFINITY;  // reference max of P and O (base-2 units)
     float l = 0.f;
     bool ok = true;
+    const T* mrow = nullptr;
+    if constexpr (MASK)  // rows past Sq (a ragged last tile) read row Sq - 1; their output is dropped
+      mrow = reinterpret_cast<const T*>(p.mask) + (int64_t)b * p.m_b + (int64_t)hq * p.m_h +
+             (int64_t)min(row, p.Sq - 1) * p.m_q;
     for (int j = 0; j < nkv_mine; ++j) {
+      const int k0 = j * BLK;
+      // MASK: the block's 128 mask values of the row, loaded before the wait for S (which hides
+      // their latency), folded into the scores chunk by chunk below
+      uint32_t mk[MASK ? 64 : 1];
+      if constexpr (MASK) load_mask_row<T>(mrow, k0, p.Skv, p.mask_vec != 0, mk);
       if (!sm100::mbar_wait(&s_full[t], (uint32_t)(j & 1), abort_flag, p.err)) { ok = false; break; }
       sm100::tc_fence_after();
-      const int k0 = j * BLK;
       const bool need_mask = (k0 + BLK - 1 > kmax);
-      // The row's 128 scores: four TMEM loads in flight, one wait.
       uint32_t sr[4][32];
+      if constexpr (!MASK) {
+        // The row's 128 scores: four TMEM loads in flight, one wait.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, sr[c]);
-      sm100::tmem_ld_wait();
+        for (int c = 0; c < 4; ++c) sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, sr[c]);
+        sm100::tmem_ld_wait();
+      } else {
+        // scores as base-2 logits u = S * scale * log2e + mask * log2e, one TMEM chunk at a time
+        // so the mask registers free as the scores arrive
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          sm100::tmem_ld_32x32b_x32(s_tmem + c * 32, sr[c]);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const uint32_t w = mk[c * 16 + (i >> 1)];
+            const float mv = widen16<T>((i & 1) ? (w >> 16) : (w & 0xFFFFu));
+            sr[c][i] = __float_as_uint(fmaf(__uint_as_float(sr[c][i]), p.scale_log2, mv * kLog2e));
+          }
+        }
+      }
       if (need_mask) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -390,7 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mx8[k] = fmaxf(m, __uint_as_float(v[15]));
       }
       const float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-      const float m_blk = mx * p.scale_log2;
+      // (unmasked: the max of S times the scale, which the host only allows to be positive)
+      const float m_blk = MASK ? mx : mx * p.scale_log2;
       // Rescale O and l only when the max grows by more than the threshold (done after P is
       // written, before P is published: PV_t(j) must accumulate into the rescaled O).
       const bool grow = m_blk > m_used + kRescaleThreshold;
@@ -400,7 +466,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns, the
       // argument in packed fp32x2; the fp32 probabilities stay in sr for the row sum, which is
       // taken after P is published (off the path to the next MMA)
-      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_ref, -m_ref);
+      const float2 sc2 = MASK ? make_float2(1.f, 1.f) : make_float2(p.scale_log2, p.scale_log2);
+      const float2 nm2 = make_float2(-m_ref, -m_ref);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
@@ -585,7 +652,7 @@ __global__ void __launch_bounds__(128) attn_generic_kernel(GenArgs a, Params p) 
 }
 
 // ---------------------------------------------------------------------------- host -------
-template <typename T, int D>
+template <typename T, int D, bool MASK>
 int launch_tc(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, Params p, CUtensorMapDataType tdt,
               cudaStream_t st) {
   using S = Smem<D>;
@@ -608,7 +675,7 @@ int launch_tc(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, Params
   if ((rc = tma::encode_4d(&tv, tdt, v->data, p.D, p.Skv, p.Hkv, p.B, sb(v, 2), sb(v, 1), sb(v, 0), 64, BLK)) !=
       NTB_OK)
     return rc;
-  auto kernel = attn_tc_kernel<T, D>;
+  auto kernel = attn_tc_kernel<T, D, MASK>;
   {
     // The register split assumes the compiled launch register count (kLaunchRegs).
     static std::atomic<int> regs_ok{0};
@@ -722,16 +789,38 @@ extern "C" int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor*
   cudaStream_t st = (cudaStream_t)stream;
   const bool half_t = q->dtype == NTB_BF16 || q->dtype == NTB_F16;
   const int es = dtype_size(q->dtype);
-  const bool tc = half_t && mask == nullptr && (p.D == 64 || p.D == 128) && v->shape[3] == p.D && p.Skv > 0 &&
-                  tma_attn_ok(q, es) && tma_attn_ok(k, es) && tma_attn_ok(v, es) &&
-                  (reinterpret_cast<uintptr_t>(o->data) % 16 == 0) && (p.o_s % 8 == 0) &&
+  // Additive masks run on the tensor cores when their key stride is 1; 16-byte mask loads when
+  // every row segment is aligned (broadcast dimensions have stride 0).
+  const bool mask_tc = mask == nullptr || mask->stride[3] == 1 || mask->shape[3] == 1;
+  if (mask != nullptr) {
+    p.mask = mask->data;
+    p.m_b = mask->shape[0] == 1 ? 0 : mask->stride[0];
+    p.m_h = mask->shape[1] == 1 ? 0 : mask->stride[1];
+    p.m_q = mask->shape[2] == 1 ? 0 : mask->stride[2];
+    p.mask_vec = reinterpret_cast<uintptr_t>(mask->data) % 16 == 0 && (p.m_b * es) % 16 == 0 &&
+                 (p.m_h * es) % 16 == 0 && (p.m_q * es) % 16 == 0;
+  }
+  // Without a mask the kernel takes the max of the raw scores and scales it, which needs a
+  // positive scale; with a mask it works on the scaled logits, whatever the scale's sign.
+  const bool tc = half_t && mask_tc && (mask != nullptr || scale > 0.0) && (p.D == 64 || p.D == 128) &&
+                  v->shape[3] == p.D && p.Skv > 0 && tma_attn_ok(q, es) && tma_attn_ok(k, es) &&
+                  tma_attn_ok(v, es) && (reinterpret_cast<uintptr_t>(o->data) % 16 == 0) && (p.o_s % 8 == 0) &&
                   (p.o_h % 8 == 0 || p.Hq == 1) && (p.o_b % 8 == 0 || p.B == 1);
   if (tc) {
-    if (q->dtype == NTB_BF16)
-      return p.D == 128 ? launch_tc<__nv_bfloat16, 128>(q, k, v, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st)
-                        : launch_tc<__nv_bfloat16, 64>(q, k, v, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
-    return p.D == 128 ? launch_tc<__half, 128>(q, k, v, p, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st)
-                      : launch_tc<__half, 64>(q, k, v, p, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
+    const bool bf = q->dtype == NTB_BF16;
+    const CUtensorMapDataType tdt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (mask != nullptr) {
+      if (bf)
+        return p.D == 128 ? launch_tc<__nv_bfloat16, 128, true>(q, k, v, p, tdt, st)
+                          : launch_tc<__nv_bfloat16, 64, true>(q, k, v, p, tdt, st);
+      return p.D == 128 ? launch_tc<__half, 128, true>(q, k, v, p, tdt, st)
+                        : launch_tc<__half, 64, true>(q, k, v, p, tdt, st);
+    }
+    if (bf)
+      return p.D == 128 ? launch_tc<__nv_bfloat16, 128, false>(q, k, v, p, tdt, st)
+                        : launch_tc<__nv_bfloat16, 64, false>(q, k, v, p, tdt, st);
+    return p.D == 128 ? launch_tc<__half, 128, false>(q, k, v, p, tdt, st)
+                      : launch_tc<__half, 64, false>(q, k, v, p, tdt, st);
   }
   NTB_DISPATCH_FLOAT(q->dtype, return launch_generic<scalar_t>(q, k, v, mask, p, (int)v->shape[3], st));
   return NTB_OK;

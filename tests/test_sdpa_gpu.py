@@ -129,3 +129,54 @@ def test_asserts_like_reference():
         nt.scaled_dot_product_attention(q, k, k)  # GQA shapes without enable_gqa
     with pytest.raises(AssertionError):
         nt.scaled_dot_product_attention(q, q, q, dropout_p=0.1)
+
+
+# Additive / bool masks on the tensor-core kernel (bf16 / fp16, head_dim 64 / 128, more than 16
+# query rows so the decode kernel is not taken): broadcast and per-head masks, ragged lengths,
+# GQA, rows whose every key is masked (NaN, as torch), and negative scales.
+MASK_TC_CASES = [
+    # b, hq, hkv, sq, skv, d, dtype, mask_kind, scale
+    (1, 4, 4, 256, 256, 128, torch.bfloat16, "bool_2d", None),
+    (2, 8, 2, 300, 517, 128, torch.bfloat16, "float_per_head", None),
+    (1, 2, 1, 129, 1000, 64, torch.float16, "float_2d", None),
+    (2, 4, 4, 384, 384, 64, torch.bfloat16, "bool_per_batch", 0.3),
+    (1, 4, 2, 200, 333, 128, torch.float16, "float_per_head", -0.08),
+    (1, 2, 2, 256, 256, 128, torch.bfloat16, "rows_fully_masked", None),
+]
+
+
+@pytest.mark.parametrize("b,hq,hkv,sq,skv,d,dtype,mask_kind,scale", MASK_TC_CASES)
+def test_masked_attention_tensor_core(b, hq, hkv, sq, skv, d, dtype, mask_kind, scale):
+    g = torch.Generator().manual_seed(sq * 7 + skv)
+    q = torch.randn((b, hq, sq, d), generator=g).to(dtype)
+    k = torch.randn((b, hkv, skv, d), generator=g).to(dtype)
+    v = torch.randn((b, hkv, skv, d), generator=g).to(dtype)
+    keep = None
+    if mask_kind == "bool_2d":
+        mask = torch.rand((sq, skv), generator=g) > 0.3
+    elif mask_kind == "bool_per_batch":
+        mask = torch.rand((b, 1, sq, skv), generator=g) > 0.5
+    elif mask_kind == "float_2d":
+        mask = torch.where(torch.rand((sq, skv), generator=g) > 0.4, 0.0, float("-inf")).to(dtype)
+    elif mask_kind == "float_per_head":
+        mask = (torch.randn((b, hq, sq, skv), generator=g) * 2).to(dtype)
+        mask[..., ::7] = float("-inf")
+    else:  # every key of some rows masked
+        keep = torch.rand((sq, skv), generator=g) > 0.3
+        keep[::5] = False
+        mask = keep
+    got = nt.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV), attn_mask=mask.to(DEV), scale=scale,
+                                          enable_gqa=True)
+    want = O.scaled_dot_product_attention(q, k, v, mask, False, scale)
+    assert_close(got, want, tol=(2.5e-2, 2.5e-2), equal_nan=True)
+    if keep is not None:
+        assert torch.isnan(got[:, :, ::5].float()).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_negative_scale_without_mask(dtype):
+    # the unmasked tensor-core kernel needs a positive scale; a negative one runs elsewhere
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn((1, 2, 256, 128), generator=g).to(dtype) for _ in range(3))
+    got = nt.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV), scale=-0.05)
+    assert_close(got, O.scaled_dot_product_attention(q, k, v, None, False, -0.05), tol=(2.5e-2, 2.5e-2))
