@@ -53,9 +53,9 @@ GLOBAL_BATCH = 16
 SEQ = 2048
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) of one launch of the fused gate/up (SwiGLU) projection at the full
-# chain size: ncu dram__bytes_read.sum 4.700038 GB + dram__bytes_write.sum 0.932619 GB
-# (profiles/gemm_tc_pair_kernel-swiglu_32768x28672x4096_bf16.md).
-SWIGLU_GEMM_TRAFFIC = 5_632_656_752
+# chain size: ncu dram__bytes_read.sum 5.720481 GB + dram__bytes_write.sum 0.931596 GB with A
+# loaded evict-last (profiles/gemm_tc_pair_kernel-swiglu_32768x28672x4096_bf16.md).
+SWIGLU_GEMM_TRAFFIC = 6_652_076_800
 
 
 def host_threads():

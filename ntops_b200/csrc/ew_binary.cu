@@ -92,7 +92,12 @@ extern "C" int ntb_binary(int op, const NtbTensor* a, const NtbTensor* b, const 
         return ew::launch<2, nbool, nbool>(ops::Mul{}, xs, y, st);
       }
       return run_arith(ops::Mul{}, a, b, y, st, true);
-    case NTB_BIN_DIV: return run_arith(ops::Div{}, a, b, y, st, false);
+    case NTB_BIN_DIV:
+      if (a->dtype == NTB_BF16 && y->dtype == a->dtype) {  // fp16's IEEE path already runs 4 blocks / SM
+        const NtbTensor* xs[2] = {a, b};
+        return ew::launch<2, __nv_bfloat16, __nv_bfloat16>(ops::DivFast16{}, xs, y, st);
+      }
+      return run_arith(ops::Div{}, a, b, y, st, false);
     case NTB_BIN_DIV_TRUNC: return run_arith(ops::DivTrunc{}, a, b, y, st, true);
     case NTB_BIN_DIV_FLOOR: return run_arith(ops::DivFloor{}, a, b, y, st, true);
     case NTB_BIN_POW:
