@@ -225,9 +225,11 @@ NTB_API int ntb_gemm_rope(const NtbTensor* a, const NtbTensor* w, const NtbTenso
  * x[n, c, p*sh - ph + r*dh, q*sw - pw + s*dw] (zero outside the input).  x: [N, C, H, W] and
  * w: [K, C, R, S] (any strides), b: NULL or [K], y: [N, K, P, Q] contiguous per image;
  * params = {stride_h, stride_w, padding_h, padding_w, dilation_h, dilation_w}; precision as in
- * ntb_gemm (fp32 operands).  `workspace`: caller-allocated device memory of at least
- * ntb_conv2d_workspace() bytes, 256-byte aligned (the patch matrix of one image and the
- * reshaped weight).  Replaces torch/conv2d.py:8-52 + kernels/conv2d.py:16-115. */
+ * ntb_gemm (fp32 operands).  `workspace`: caller-allocated device memory, 256-byte aligned.
+ * ntb_conv2d_workspace() reports the recommended size (the reshaped weight and the patch
+ * matrices of up to 256 MiB of images); any size that holds the weight and one image's patch
+ * matrix is accepted, and the images then run in as many batched GEMMs as the room requires.
+ * Replaces torch/conv2d.py:8-52 + kernels/conv2d.py:16-115. */
 NTB_API int ntb_conv2d_workspace(const NtbTensor* x, const NtbTensor* w, const int* params, int64_t* bytes);
 NTB_API int ntb_conv2d(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTensor* y,
                        const int* params, int precision, void* workspace, int64_t workspace_bytes, void* stream);

@@ -1,16 +1,19 @@
-// ntb_conv2d: 2-D convolution as im2col + the tcgen05 GEMM, one GEMM per image.
+// ntb_conv2d: 2-D convolution as im2col + one batched tcgen05 GEMM per chunk of images.
 //
 // Reference (ntops kernels/conv2d.py:16-115, torch/conv2d.py:8-52): the padded input is tiled
 // into (C, R, S) patches with the given stride / dilation and multiplied with the weight
 // flattened to [K, C*R*S] by the mm kernel, bias added in the epilogue, NCHW output; groups = 1.
-// Here, per image n: a gather kernel writes the patch matrix col[(c, r, s), (p, q)] (zeros where
-// the window leaves the input) into a caller-provided workspace, and the product
-//   y[n] (as [K, P*Q]) = W [K, C*R*S] x col [C*R*S, P*Q] + bias[k]
-// runs on the GEMM of gemm_sm100.cu (tcgen05 for fp16 / bf16, the fp64-accumulating CUDA-core
-// path for fp32 as the reference's default IEEE precision asks).  The output lands in NCHW
-// directly (row k of the product is channel k of image n).  The patch rows are padded to a
-// multiple of 8 elements (and the weight copied with zero columns to match) so every GEMM
-// operand row is 16-byte aligned for TMA.
+// Here the images run in chunks of nb: a gather kernel writes, for each image n of the chunk,
+// the patch matrix col[n][(c, r, s), (p, q)] (zeros where the window leaves the input) into a
+// caller-provided workspace, and one batched product
+//   y[n] (as [K, P*Q]) = W [K, C*R*S] x col[n] [C*R*S, P*Q] + bias[k],   n in the chunk
+// runs on the GEMM of gemm_sm100.cu with the packed weight broadcast over the batch (batch
+// stride 0, so every tile re-reads it from L2), tcgen05 for fp16 / bf16 and the fp64-accumulating
+// CUDA-core path for fp32 as the reference's default IEEE precision asks.  The output lands in
+// NCHW directly (row k of image n's product is channel k of image n).  The patch rows are padded
+// to a multiple of 8 elements (and the weight copied with zero columns to match) so every GEMM
+// operand row is 16-byte aligned for TMA.  One batched GEMM over many images fills the 148 SMs
+// where a per-image product of a small layer covers a fraction of them.
 #include "elementwise.cuh"
 
 namespace ntb {
@@ -23,21 +26,45 @@ struct ConvGeom {
   int64_t xs[4];  // input strides (n, c, h, w) in elements
 };
 
+// Patch matrices of nb images: col[n] is [crs_pad, pq_pad] at col + n * crs_pad * pq_pad.
+// Block (x, row, n) writes 8 consecutive (p, q) columns per thread of patch row `row` of image
+// n as 16-byte stores; the (c, r, s) decomposition is done once per block.
 template <typename T>
-__global__ void __launch_bounds__(256) im2col_kernel(const T* __restrict__ x, T* __restrict__ col, ConvGeom g,
-                                                     int64_t total) {
-  // col is [crs_pad, pq_pad]; element (row, j): row = (c, r, s), j = (p, q)
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int row = (int)(i / g.pq_pad);
-    const int j = (int)(i - (int64_t)row * g.pq_pad);
-    T v = cvt<T>(0.f);
-    if (row < g.crs && j < g.P * g.Q) {
-      const int c = row / (g.R * g.S), rs = row % (g.R * g.S), r = rs / g.S, s = rs % g.S;
-      const int p = j / g.Q, q = j % g.Q;
-      const int hi = p * g.sh - g.ph + r * g.dh, wi = q * g.sw - g.pw + s * g.dw;
-      if (hi >= 0 && hi < g.H && wi >= 0 && wi < g.W) v = x[c * g.xs[1] + hi * g.xs[2] + wi * g.xs[3]];
+__global__ void __launch_bounds__(256) im2col_kernel(const T* __restrict__ x, T* __restrict__ col, ConvGeom g) {
+  const int row = blockIdx.y;
+  const int n = blockIdx.z;
+  const T* xn = x + (int64_t)n * g.xs[0];
+  T* dst = col + ((int64_t)n * g.crs_pad + row) * g.pq_pad;
+  const bool live = row < g.crs;
+  int c = 0, r = 0, s = 0;
+  if (live) {
+    c = row / (g.R * g.S);
+    const int rs = row - c * (g.R * g.S);
+    r = rs / g.S;
+    s = rs - r * g.S;
+  }
+  const int pq = g.P * g.Q;
+  const T* xc = xn + (int64_t)c * g.xs[1];
+  for (int j0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8; j0 < g.pq_pad; j0 += gridDim.x * blockDim.x * 8) {
+    alignas(16) T v[8];
+    int p = j0 / g.Q, q = j0 - p * g.Q;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      T t = cvt<T>(0.f);
+      if (live && j0 + e < pq) {
+        const int hi = p * g.sh - g.ph + r * g.dh, wi = q * g.sw - g.pw + s * g.dw;
+        if (hi >= 0 && hi < g.H && wi >= 0 && wi < g.W) t = xc[hi * g.xs[2] + wi * g.xs[3]];
+      }
+      v[e] = t;
+      if (++q == g.Q) {
+        q = 0;
+        ++p;
+      }
     }
-    col[i] = v;
+    const uint4* src = reinterpret_cast<const uint4*>(v);
+    uint4* out = reinterpret_cast<uint4*>(dst + j0);
+#pragma unroll
+    for (int k = 0; k < (int)(8 * sizeof(T) / 16); ++k) out[k] = src[k];
   }
 }
 
@@ -63,6 +90,13 @@ int grid_for(int64_t total) {
   return (int)(g < 1 ? 1 : (g > cap ? cap : g));
 }
 
+// Patch matrices the recommended workspace holds at most: 256 MiB, so a large batch runs in a
+// few chunks (each one batched GEMM of several waves) instead of one patch copy of every image.
+constexpr int64_t kColBudget = 256ll << 20;
+
+int64_t weight_bytes(const ConvGeom& g, int es) { return ((int64_t)g.K * g.crs_pad * es + 255) / 256 * 256; }
+int64_t image_bytes(const ConvGeom& g, int es) { return (int64_t)g.crs_pad * g.pq_pad * es; }
+
 int plan(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTensor* y, const int* prm,
          ConvGeom* g, int64_t* ws_bytes) {
   int rc;
@@ -75,6 +109,7 @@ int plan(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTe
           (long long)w->shape[1], (long long)x->shape[1]);
   NTB_UNSUP(w->dtype == x->dtype && dtype_is_float(x->dtype), "input and weight must share one floating dtype");
   for (int i = 0; i < 6; ++i) NTB_ARG(prm[i] >= (i >= 2 && i < 4 ? 0 : 1), "bad stride / padding / dilation");
+  NTB_ARG(x->shape[0] < 65536, "at most 65535 images");
   g->C = (int)x->shape[1];
   g->H = (int)x->shape[2];
   g->W = (int)x->shape[3];
@@ -90,6 +125,7 @@ int plan(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTe
   g->crs = g->C * g->R * g->S;
   g->crs_pad = (g->crs + 7) / 8 * 8;
   g->pq_pad = (int)((P * Q + 7) / 8 * 8);
+  NTB_ARG(g->crs_pad < 65536, "C * R * S must stay below 65536");
   for (int i = 0; i < 4; ++i) g->xs[i] = x->stride[i];
   if (y != nullptr) {
     NTB_ARG(y->ndim == 4 && y->shape[0] == x->shape[0] && y->shape[1] == g->K && y->shape[2] == P && y->shape[3] == Q,
@@ -102,43 +138,52 @@ int plan(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTe
     NTB_UNSUP(b->dtype == x->dtype, "bias dtype must equal the input dtype");
   }
   const int es = dtype_size(x->dtype);
-  const int64_t wbytes = ((int64_t)g->K * g->crs_pad * es + 255) / 256 * 256;
-  *ws_bytes = wbytes + (int64_t)g->crs_pad * g->pq_pad * es;
+  const int64_t per = image_bytes(*g, es);
+  int64_t nb = kColBudget / (per > 0 ? per : 1);
+  nb = nb < 1 ? 1 : (nb > x->shape[0] ? x->shape[0] : nb);
+  *ws_bytes = weight_bytes(*g, es) + (nb < 1 ? 1 : nb) * per;
   return NTB_OK;
 }
 
-NtbTensor view2d(void* data, int dtype, int64_t rows, int64_t cols, int64_t rs, int64_t cs) {
+NtbTensor view3d(void* data, int dtype, int64_t n, int64_t rows, int64_t cols, int64_t ns, int64_t rs, int64_t cs) {
   NtbTensor t{};
   t.data = data;
   t.dtype = dtype;
-  t.ndim = 2;
-  t.shape[0] = rows;
-  t.shape[1] = cols;
-  t.stride[0] = rs;
-  t.stride[1] = cs;
+  t.ndim = 3;
+  t.shape[0] = n;
+  t.shape[1] = rows;
+  t.shape[2] = cols;
+  t.stride[0] = ns;
+  t.stride[1] = rs;
+  t.stride[2] = cs;
   return t;
 }
 
+// nb_max: images whose patch matrices fit the workspace after the packed weight.
 template <typename T>
 int run(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTensor* y, const ConvGeom& g,
-        uint8_t* ws, int precision, cudaStream_t st) {
+        uint8_t* ws, int64_t nb_max, int precision, cudaStream_t st) {
   const int es = sizeof(T);
-  const int64_t wbytes = ((int64_t)g.K * g.crs_pad * es + 255) / 256 * 256;
   T* wp = reinterpret_cast<T*>(ws);
-  T* col = reinterpret_cast<T*>(ws + wbytes);
+  T* col = reinterpret_cast<T*>(ws + weight_bytes(g, es));
   pack_weight_kernel<T><<<grid_for((int64_t)g.K * g.crs_pad), 256, 0, st>>>(
       (const T*)w->data, wp, g, w->stride[0], w->stride[1], w->stride[2], w->stride[3]);
   NTB_LAUNCH_CHECK();
-  const int64_t total = (int64_t)g.crs_pad * g.pq_pad;
   const int64_t PQ = (int64_t)g.P * g.Q;
-  NtbTensor A = view2d(wp, x->dtype, g.K, g.crs_pad, g.crs_pad, 1);
-  NtbTensor B = view2d(col, x->dtype, g.crs_pad, PQ, g.pq_pad, 1);
-  NtbTensor bias;
-  if (b != nullptr) bias = view2d(b->data, x->dtype, g.K, PQ, b->stride[0], 0);
-  for (int64_t n = 0; n < x->shape[0]; ++n) {
-    im2col_kernel<T><<<grid_for(total), 256, 0, st>>>((const T*)x->data + n * x->stride[0], col, g, total);
+  const int64_t per = (int64_t)g.crs_pad * g.pq_pad;
+  const int64_t N = x->shape[0];
+  const unsigned gx = (unsigned)((g.pq_pad / 8 + 255) / 256);
+  for (int64_t n0 = 0; n0 < N; n0 += nb_max) {
+    const int64_t nb = N - n0 < nb_max ? N - n0 : nb_max;
+    im2col_kernel<T><<<dim3(gx, (unsigned)g.crs_pad, (unsigned)nb), 256, 0, st>>>(
+        (const T*)x->data + n0 * x->stride[0], col, g);
     NTB_LAUNCH_CHECK();
-    NtbTensor D = view2d((T*)y->data + n * y->stride[0], x->dtype, g.K, PQ, PQ, 1);
+    // The weight is broadcast over the chunk (batch stride 0); so is the bias, along rows.
+    NtbTensor A = view3d(wp, x->dtype, nb, g.K, g.crs_pad, 0, g.crs_pad, 1);
+    NtbTensor B = view3d(col, x->dtype, nb, g.crs_pad, PQ, per, g.pq_pad, 1);
+    NtbTensor D = view3d((T*)y->data + n0 * y->stride[0], x->dtype, nb, g.K, PQ, y->stride[0], PQ, 1);
+    NtbTensor bias;
+    if (b != nullptr) bias = view3d(b->data, x->dtype, nb, g.K, PQ, 0, b->stride[0], 0);
     const int rc = ntb_gemm(&A, &B, b != nullptr ? &bias : nullptr, &D, 1.0, b != nullptr ? 1.0 : 0.0, precision, st);
     if (rc != NTB_OK) return rc;
   }
@@ -165,10 +210,16 @@ extern "C" int ntb_conv2d(const NtbTensor* x, const NtbTensor* w, const NtbTenso
   int rc = plan(x, w, b, y, params, &g, &need);
   if (rc != NTB_OK) return rc;
   if (x->shape[0] == 0 || g.K == 0) return NTB_OK;
-  NTB_ARG(workspace != nullptr && workspace_bytes >= need, "workspace too small: need %lld bytes", (long long)need);
+  // Any workspace that holds the packed weight and one image's patch matrix works; more room
+  // (up to the size ntb_conv2d_workspace reports) runs more images per batched GEMM.
+  const int es = dtype_size(x->dtype);
+  const int64_t least = weight_bytes(g, es) + image_bytes(g, es);
+  NTB_ARG(workspace != nullptr && workspace_bytes >= least, "workspace too small: need %lld bytes (%lld recommended)",
+          (long long)least, (long long)need);
   NTB_ARG(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "workspace must be 256-byte aligned");
+  const int64_t nb_max = (workspace_bytes - weight_bytes(g, es)) / image_bytes(g, es);
   cudaStream_t st = (cudaStream_t)stream;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  NTB_DISPATCH_FLOAT(x->dtype, return run<scalar_t>(x, w, b, y, g, ws, precision, st));
+  NTB_DISPATCH_FLOAT(x->dtype, return run<scalar_t>(x, w, b, y, g, ws, nb_max, precision, st));
   return NTB_OK;
 }

@@ -8,8 +8,9 @@
 // (seed low word, seed high word); the first output word, read as int32 x, becomes
 // (x < 0 ? -x - 1 : x) * 4.6566127342e-10 in fp32 (Triton 3.6 language/random.py).  The keep
 // test and the scaling are done in fp64 as the reference's fp64 `p` makes them, so the mask and
-// the values match the reference's for the same seed.  Philox costs ~10 x 8 integer operations
-// per element, so the kernel is issue-bound rather than HBM-bound.
+// the values match the reference's for the same seed.  One Philox evaluation per element (the
+// reference's tl.rand keeps the first of its four words) costs 20 wide multiplies and 20 xors,
+// so the kernel is bound by integer issue rather than by HBM.
 #include "elementwise.cuh"
 
 namespace ntb {
@@ -22,11 +23,12 @@ __device__ __forceinline__ float philox_uniform(uint64_t offset, uint32_t k0, ui
   uint32_t c0 = (uint32_t)offset, c1 = (uint32_t)(offset >> 32), c2 = 0u, c3 = 0u;
 #pragma unroll
   for (int r = 0; r < 10; ++r) {
-    const uint32_t a = c0, b = c2;
-    c0 = __umulhi(kPhiloxRoundB, b) ^ c1 ^ k0;
-    c2 = __umulhi(kPhiloxRoundA, a) ^ c3 ^ k1;
-    c1 = kPhiloxRoundB * b;
-    c3 = kPhiloxRoundA * a;
+    // one 32 x 32 -> 64-bit product gives both halves a round needs
+    const uint64_t pb = (uint64_t)kPhiloxRoundB * c2, pa = (uint64_t)kPhiloxRoundA * c0;
+    c0 = (uint32_t)(pb >> 32) ^ c1 ^ k0;
+    c2 = (uint32_t)(pa >> 32) ^ c3 ^ k1;
+    c1 = (uint32_t)pb;
+    c3 = (uint32_t)pa;
     k0 += kPhiloxKeyA;
     k1 += kPhiloxKeyB;
   }
@@ -35,9 +37,11 @@ __device__ __forceinline__ float philox_uniform(uint64_t offset, uint32_t k0, ui
   return (float)x * 4.6566127342e-10f;
 }
 
+// The keep test (double)r > p is done as r > pf in fp32, pf the largest float not above p: no
+// float lies strictly between pf and p's successor float, so the two tests agree for every r.
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) dropout_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n,
-                                                      double p, double q, uint32_t k0, uint32_t k1) {
+                                                      float pf, double q, uint32_t k0, uint32_t k1) {
   const int64_t nvec = n / VEC;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
@@ -46,14 +50,14 @@ __global__ void __launch_bounds__(256) dropout_kernel(const T* __restrict__ x, T
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
       const float r = philox_uniform((uint64_t)(v * VEC + e), k0, k1);
-      o.v[e] = (double)r > p ? cvt<T>(cvt<double>(xv.v[e]) / q) : cvt<T>(0.0);
+      o.v[e] = r > pf ? cvt<T>(cvt<double>(xv.v[e]) / q) : cvt<T>(0.0);
     }
     ew::store_cs(reinterpret_cast<ew::Vec<T, VEC>*>(y) + v, o);
   }
   // tail (n not a multiple of VEC): one thread per element
   for (int64_t i = nvec * VEC + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     const float r = philox_uniform((uint64_t)i, k0, k1);
-    y[i] = (double)r > p ? cvt<T>(cvt<double>(x[i]) / q) : cvt<T>(0.0);
+    y[i] = r > pf ? cvt<T>(cvt<double>(x[i]) / q) : cvt<T>(0.0);
   }
 }
 
@@ -61,6 +65,8 @@ template <typename T>
 int launch_dropout(const NtbTensor* x, const NtbTensor* y, int64_t n, double p, uint64_t seed, cudaStream_t st) {
   const uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
   const double q = 1.0 - p;
+  float pf = (float)p;  // round to nearest, then step down if that landed above p
+  if ((double)pf > p) pf = nextafterf(pf, -1.0f);
   constexpr int V = ew::vec_elems<T>();
   const bool vec = ew::aligned(x->data, 16) && ew::aligned(y->data, 16);
   const int64_t items = vec ? n / V : n;
@@ -69,9 +75,9 @@ int launch_dropout(const NtbTensor* x, const NtbTensor* y, int64_t n, double p, 
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
   if (vec)
-    dropout_kernel<T, V><<<(unsigned)grid, 256, 0, st>>>((const T*)x->data, (T*)y->data, n, p, q, k0, k1);
+    dropout_kernel<T, V><<<(unsigned)grid, 256, 0, st>>>((const T*)x->data, (T*)y->data, n, pf, q, k0, k1);
   else
-    dropout_kernel<T, 1><<<(unsigned)grid, 256, 0, st>>>((const T*)x->data, (T*)y->data, n, p, q, k0, k1);
+    dropout_kernel<T, 1><<<(unsigned)grid, 256, 0, st>>>((const T*)x->data, (T*)y->data, n, pf, q, k0, k1);
   NTB_LAUNCH_CHECK();
   return NTB_OK;
 }

@@ -49,6 +49,8 @@ struct Params {
   int M, N, K, batch;
   int mblocks, nblocks, kblocks, tiles;
   int a_mn, b_mn;  // operand is MN-major (else K-major)
+  int a_bcast, b_bcast;  // operand broadcast over the batch (batch stride 0): its tensor map holds
+                         // one batch and every tile loads batch 0
   int band;        // M-blocks per raster band (power of two)
   void* d;
   int64_t d_bs, d_ms;  // output: batch and row strides (unit column stride)
@@ -298,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
         int b, mb, nb;
         tile_coords(tile, p, b, mb, nb);
+        const int ba = p.a_bcast ? 0 : b, bb = p.b_bcast ? 0 : b;  // broadcast operands load batch 0
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!sm100::mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
             ok = false;
@@ -309,18 +312,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* a_dst = sA + stage * S::A_BYTES;
           uint8_t* b_dst = sB + stage * S::B_BYTES;
           if (!p.a_mn) {
-            sm100::tma_load_3d(a_dst, &tma_a, &full[stage], kb * BK, mb * BM, b);
+            sm100::tma_load_3d(a_dst, &tma_a, &full[stage], kb * BK, mb * BM, ba);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j)
-              sm100::tma_load_3d(a_dst + j * BK * kRowBytes, &tma_a, &full[stage], mb * BM + j * 64, kb * BK, b);
+              sm100::tma_load_3d(a_dst + j * BK * kRowBytes, &tma_a, &full[stage], mb * BM + j * 64, kb * BK, ba);
           }
           if (!p.b_mn) {
-            sm100::tma_load_3d(b_dst, &tma_b, &full[stage], kb * BK, nb * BN, b);
+            sm100::tma_load_3d(b_dst, &tma_b, &full[stage], kb * BK, nb * BN, bb);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              sm100::tma_load_3d(b_dst + j * BK * kRowBytes, &tma_b, &full[stage], nb * BN + j * 64, kb * BK, b);
+              sm100::tma_load_3d(b_dst + j * BK * kRowBytes, &tma_b, &full[stage], nb * BN + j * 64, kb * BK, bb);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -512,6 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = pair; ok && tile < p.tiles; tile += npairs) {
         int b, mb, nb;
         tile_coords(tile, p, b, mb, nb);
+        const int ba = p.a_bcast ? 0 : b, bb = p.b_bcast ? 0 : b;  // broadcast operands load batch 0
         const int row0 = mb * kPairBM + (int)rank * BM;
         const int col0 = nb * BN + (int)rank * (BN / 2);
         for (int kb = 0; kb < p.kblocks; ++kb) {
@@ -528,18 +532,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* a_dst = sA + stage * S::A_BYTES;
           uint8_t* b_dst = sB + stage * S::B_BYTES;
           if (!p.a_mn) {
-            sm100::tma_load_3d_pair_hint(a_dst, &tma_a, bar, kb * BK, row0, b, pol_a);
+            sm100::tma_load_3d_pair_hint(a_dst, &tma_a, bar, kb * BK, row0, ba, pol_a);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j)
-              sm100::tma_load_3d_pair_hint(a_dst + j * BK * kRowBytes, &tma_a, bar, row0 + j * 64, kb * BK, b, pol_a);
+              sm100::tma_load_3d_pair_hint(a_dst + j * BK * kRowBytes, &tma_a, bar, row0 + j * 64, kb * BK, ba,
+                                           pol_a);
           }
           if (!p.b_mn) {
-            sm100::tma_load_3d_pair_hint(b_dst, &tma_b, bar, kb * BK, col0, b, pol_b);
+            sm100::tma_load_3d_pair_hint(b_dst, &tma_b, bar, kb * BK, col0, bb, pol_b);
           } else {
 #pragma unroll
             for (int j = 0; j < (BN / 2) / 64; ++j)
-              sm100::tma_load_3d_pair_hint(b_dst + j * BK * kRowBytes, &tma_b, bar, col0 + j * 64, kb * BK, b, pol_b);
+              sm100::tma_load_3d_pair_hint(b_dst + j * BK * kRowBytes, &tma_b, bar, col0 + j * 64, kb * BK, bb,
+                                           pol_b);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -724,18 +730,19 @@ int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& 
   CUtensorMap ta, tb;
   int rc;
   const uint64_t B = (uint64_t)p.batch;
+  const uint64_t BA = p.a_bcast ? 1 : B, BB = p.b_bcast ? 1 : B;
   // A: K-major -> dims (K, M, B), box (BK, BM); MN-major -> dims (M, K, B), box (64, BK).
   if (!p.a_mn)
-    rc = tma::encode_3d(&ta, tdt, a->data, p.K, p.M, B, oa.s_outer * es, (B > 1 ? oa.bs : oa.s_outer * p.M) * es,
+    rc = tma::encode_3d(&ta, tdt, a->data, p.K, p.M, BA, oa.s_outer * es, (BA > 1 ? oa.bs : oa.s_outer * p.M) * es,
                         BK, BM);
   else
-    rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, B, oa.s_k * es, (B > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
+    rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, BA, oa.s_k * es, (BA > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
   if (rc != NTB_OK) return rc;
   if (!p.b_mn)
-    rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, B, ob.s_outer * es, (B > 1 ? ob.bs : ob.s_outer * p.N) * es,
+    rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, BB, ob.s_outer * es, (BB > 1 ? ob.bs : ob.s_outer * p.N) * es,
                         BK, BN);
   else
-    rc = tma::encode_3d(&tb, tdt, bm->data, p.N, p.K, B, ob.s_k * es, (B > 1 ? ob.bs : ob.s_k * p.K) * es, 64, BK);
+    rc = tma::encode_3d(&tb, tdt, bm->data, p.N, p.K, BB, ob.s_k * es, (BB > 1 ? ob.bs : ob.s_k * p.K) * es, 64, BK);
   if (rc != NTB_OK) return rc;
   p.kblocks = (p.K + BK - 1) / BK;
   p.mblocks = (p.M + BM - 1) / BM;
@@ -807,18 +814,19 @@ int launch_tc_pair(const NtbTensor* a, const NtbTensor* bm, Params p, const Oper
   CUtensorMap ta, tb;
   int rc;
   const uint64_t B = (uint64_t)p.batch;
+  const uint64_t BA = p.a_bcast ? 1 : B, BB = p.b_bcast ? 1 : B;
   // Each CTA loads 128 rows of A and 128 columns of B per stage.
   if (!p.a_mn)
-    rc = tma::encode_3d(&ta, tdt, a->data, p.K, p.M, B, oa.s_outer * es, (B > 1 ? oa.bs : oa.s_outer * p.M) * es,
+    rc = tma::encode_3d(&ta, tdt, a->data, p.K, p.M, BA, oa.s_outer * es, (BA > 1 ? oa.bs : oa.s_outer * p.M) * es,
                         BK, BM);
   else
-    rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, B, oa.s_k * es, (B > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
+    rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, BA, oa.s_k * es, (BA > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
   if (rc != NTB_OK) return rc;
   if (!p.b_mn)
-    rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, B, ob.s_outer * es, (B > 1 ? ob.bs : ob.s_outer * p.N) * es,
+    rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, BB, ob.s_outer * es, (BB > 1 ? ob.bs : ob.s_outer * p.N) * es,
                         BK, kPairBN / 2);
   else
-    rc = tma::encode_3d(&tb, tdt, bm->data, p.N, p.K, B, ob.s_k * es, (B > 1 ? ob.bs : ob.s_k * p.K) * es, 64, BK);
+    rc = tma::encode_3d(&tb, tdt, bm->data, p.N, p.K, BB, ob.s_k * es, (BB > 1 ? ob.bs : ob.s_k * p.K) * es, 64, BK);
   if (rc != NTB_OK) return rc;
   p.kblocks = (p.K + BK - 1) / BK;
   p.mblocks = (p.M + kPairBM - 1) / kPairBM;
@@ -908,7 +916,7 @@ bool tma_operand_ok(const NtbTensor* t, const Operand& o, bool mn_major, int64_t
   if (reinterpret_cast<uintptr_t>(t->data) % 16 != 0) return false;
   const int64_t other = mn_major ? o.s_k : o.s_outer;  // the non-unit stride
   if (!tma::stride_ok(other * es)) return false;
-  if (batch > 1 && !tma::stride_ok(o.bs * es)) return false;
+  if (batch > 1 && o.bs != 0 && !tma::stride_ok(o.bs * es)) return false;
   (void)outer;
   (void)kdim;
   return true;
@@ -964,6 +972,8 @@ extern "C" int ntb_gemm(const NtbTensor* a, const NtbTensor* bm, const NtbTensor
   if ((int64_t)p.M * p.N * p.batch == 0) return NTB_OK;
   Operand oa{ast[0], ast[1], ast[2]};
   Operand ob{bst[0], bst[2], bst[1]};
+  p.a_bcast = p.batch > 1 && oa.bs == 0;
+  p.b_bcast = p.batch > 1 && ob.bs == 0;
   cudaStream_t st = (cudaStream_t)stream;
 
   // Operand majorness: unit stride along K -> K-major, unit stride along M / N -> MN-major.

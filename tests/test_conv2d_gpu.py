@@ -51,3 +51,45 @@ def test_conv2d_valid_padding_and_strided_input():
     assert_close(got, O.conv2d(x, wt), tol=(1e-5, 1e-5))
     with pytest.raises(AssertionError):
         nt.conv2d(x.to(DEV), wt.to(DEV), groups=2)
+
+
+@pytest.mark.parametrize("dtype", (torch.bfloat16, torch.float32))
+def test_conv2d_chunked_workspace(dtype):
+    """A workspace that holds the packed weight and two patch matrices: the five images run as
+    batched GEMMs of 2, 2 and 1 images (broadcast weight, bias expanded over the batch) and
+    match the oracle and the recommended-workspace call; a workspace short of one image is
+    refused."""
+    import ctypes
+
+    from ntops_b200 import _lib as L
+
+    lib = L.load()
+    g = torch.Generator().manual_seed(3)
+    n, c, h, w, k, r = 5, 24, 19, 21, 40, 3
+    x = torch.randn((n, c, h, w), generator=g).to(dtype)
+    wt = (torch.randn((k, c, r, r), generator=g) * 0.2).to(dtype)
+    b = torch.randn((k,), generator=g).to(dtype)
+    want = O.conv2d(x, wt, b, stride=1, padding=1)
+    xd_t, wd_t, bd_t = x.to(DEV), wt.to(DEV), b.to(DEV)
+    full = nt.conv2d(xd_t, wd_t, bias=bd_t, stride=1, padding=1)
+    params = (ctypes.c_int * 6)(1, 1, 1, 1, 1, 1)
+    xd, wd, bd = L.describe(xd_t), L.describe(wd_t), L.describe(bd_t)
+    es = x.element_size()
+    crs_pad = (c * r * r + 7) // 8 * 8
+    pq_pad = (h * w + 7) // 8 * 8
+    wbytes = (k * crs_pad * es + 255) // 256 * 256
+    ws_bytes = wbytes + 2 * crs_pad * pq_pad * es + 100
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
+    y = torch.full_like(full, float("nan"))
+    yd = L.describe(y)
+    rc = lib.ntb_conv2d(ctypes.byref(xd), ctypes.byref(wd), ctypes.byref(bd), ctypes.byref(yd), params,
+                        L.PRECISION_IEEE, ctypes.c_void_p(ws.data_ptr()), ws_bytes, None)
+    torch.cuda.synchronize()
+    assert rc == L.OK
+    tol = (1e-5, 1e-5) if dtype == torch.float32 else (2e-2, 2e-2)
+    assert_close(y.cpu(), want, tol=tol)
+    assert_close(y.cpu(), full.cpu(), tol=tol)
+    small = torch.empty(wbytes + crs_pad * pq_pad * es - 16, dtype=torch.uint8, device=DEV)
+    rc = lib.ntb_conv2d(ctypes.byref(xd), ctypes.byref(wd), ctypes.byref(bd), ctypes.byref(yd), params,
+                        L.PRECISION_IEEE, ctypes.c_void_p(small.data_ptr()), small.numel(), None)
+    assert rc == L.ERR_INVALID
