@@ -227,7 +227,7 @@ NTB_API int ntb_gemm_rope(const NtbTensor* a, const NtbTensor* w, const NtbTenso
  * params = {stride_h, stride_w, padding_h, padding_w, dilation_h, dilation_w}; precision as in
  * ntb_gemm (fp32 operands).  `workspace`: caller-allocated device memory, 256-byte aligned.
  * ntb_conv2d_workspace() reports the recommended size (the reshaped weight and the patch
- * matrices of up to 256 MiB of images); any size that holds the weight and one image's patch
+ * matrices of up to 1 GiB of images); any size that holds the weight and one image's patch
  * matrix is accepted, and the images then run in as many batched GEMMs as the room requires.
  * Replaces torch/conv2d.py:8-52 + kernels/conv2d.py:16-115. */
 NTB_API int ntb_conv2d_workspace(const NtbTensor* x, const NtbTensor* w, const int* params, int64_t* bytes);

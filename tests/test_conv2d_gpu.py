@@ -93,3 +93,14 @@ def test_conv2d_chunked_workspace(dtype):
     rc = lib.ntb_conv2d(ctypes.byref(xd), ctypes.byref(wd), ctypes.byref(bd), ctypes.byref(yd), params,
                         L.PRECISION_IEEE, ctypes.c_void_p(small.data_ptr()), small.numel(), None)
     assert rc == L.ERR_INVALID
+
+
+def test_conv2d_wide_rows_gather_path():
+    """Input rows too wide for the shared-memory staged patch copy (the rows a 256-column range
+    needs exceed 48 KB) take the plain gather kernel."""
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn((2, 2, 16, 4096), generator=g)
+    wt = torch.randn((3, 2, 3, 3), generator=g)
+    b = torch.randn((3,), generator=g)
+    got = nt.conv2d(x.to(DEV), wt.to(DEV), bias=b.to(DEV), stride=4, padding=2, dilation=3)
+    assert_close(got, O.conv2d(x, wt, b, stride=4, padding=2, dilation=3), tol=(1e-5, 1e-5))
