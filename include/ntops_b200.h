@@ -225,10 +225,13 @@ NTB_API int ntb_gemm_rope(const NtbTensor* a, const NtbTensor* w, const NtbTenso
  * x[n, c, p*sh - ph + r*dh, q*sw - pw + s*dw] (zero outside the input).  x: [N, C, H, W] and
  * w: [K, C, R, S] (any strides), b: NULL or [K], y: [N, K, P, Q] contiguous per image;
  * params = {stride_h, stride_w, padding_h, padding_w, dilation_h, dilation_w}; precision as in
- * ntb_gemm (fp32 operands).  `workspace`: caller-allocated device memory, 256-byte aligned.
- * ntb_conv2d_workspace() reports the recommended size (the reshaped weight and the patch
- * matrices of up to 1 GiB of images); any size that holds the weight and one image's patch
- * matrix is accepted, and the images then run in as many batched GEMMs as the room requires.
+ * ntb_gemm (fp32 operands).  `workspace`: caller-allocated device memory, 256-byte aligned, of
+ * the size ntb_conv2d_workspace() reports.  fp16 / bf16 convolutions with at least 64 input
+ * channels run as an implicit GEMM and need exactly that size (the reshaped weight, plus a
+ * channels-innermost copy of x unless x already is channels-last).  The others build patch
+ * matrices: the reported size holds the reshaped weight and the patch matrices of up to 1 GiB of
+ * images, and any size that holds the weight and one image's patch matrix is accepted (the
+ * images then run in as many batched GEMMs as the room requires).
  * Replaces torch/conv2d.py:8-52 + kernels/conv2d.py:16-115. */
 NTB_API int ntb_conv2d_workspace(const NtbTensor* x, const NtbTensor* w, const int* params, int64_t* bytes);
 NTB_API int ntb_conv2d(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTensor* y,

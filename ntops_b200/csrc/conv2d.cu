@@ -1,19 +1,35 @@
-// ntb_conv2d: 2-D convolution as im2col + one batched tcgen05 GEMM per chunk of images.
+// ntb_conv2d: 2-D convolution on the tcgen05 GEMM, as an implicit GEMM or as im2col + GEMM.
 //
 // Reference (ntops kernels/conv2d.py:16-115, torch/conv2d.py:8-52): the padded input is tiled
 // into (C, R, S) patches with the given stride / dilation and multiplied with the weight
-// flattened to [K, C*R*S] by the mm kernel, bias added in the epilogue, NCHW output; groups = 1.
-// Here the images run in chunks of nb: a gather kernel writes, for each image n of the chunk,
-// the patch matrix col[n][(c, r, s), (p, q)] (zeros where the window leaves the input) into a
+// flattened to [K, C*R*S] by the mm kernel (an implicit arrangement: the patches are never
+// stored), bias added in the epilogue, NCHW output; groups = 1.
+//
+// Implicit GEMM (fp16 / bf16, C >= 64, paddings and filter extents inside the im2col map's
+// +-128 box corners, strides <= 8): the weight is packed tap-major, [K, (r, s, channel block of
+// 64, channel)], the input is made channels-innermost ([N, H, W, C8], skipped when the caller's
+// tensor already is), and one batched GEMM over all images computes
+//   y[n] (as [K, P*Q]) = Wtap [K, R*S*CB*64] x B_n,   B_n[(r, s, c), (p, q)] = x[n, c, p*sh - ph + r*dh, q*sw - pw + s*dw]
+// where each B tile (64 channels of one filter tap x 128 / 256 output pixels) is one TMA
+// im2col load: the copy engine walks the output pixels' window origins and fetches 64 channels
+// of the tap-shifted input pixel per row (zeros outside the input) straight into the swizzled
+// shared-memory operand layout.  The input is read from HBM about once; no patch matrix exists.
+//
+// im2col + GEMM (fp32 / fp64, fewer than 64 channels, or geometry outside those limits): the
+// images run in chunks of nb: a gather kernel writes, for each image n of the chunk, the patch
+// matrix col[n][(c, r, s), (p, q)] (zeros where the window leaves the input) into a
 // caller-provided workspace, and one batched product
 //   y[n] (as [K, P*Q]) = W [K, C*R*S] x col[n] [C*R*S, P*Q] + bias[k],   n in the chunk
 // runs on the GEMM of gemm_sm100.cu with the packed weight broadcast over the batch (batch
 // stride 0, so every tile re-reads it from L2), tcgen05 for fp16 / bf16 and the fp64-accumulating
-// CUDA-core path for fp32 as the reference's default IEEE precision asks.  The output lands in
-// NCHW directly (row k of image n's product is channel k of image n).  The patch rows are padded
-// to a multiple of 8 elements (and the weight copied with zero columns to match) so every GEMM
-// operand row is 16-byte aligned for TMA.  One batched GEMM over many images fills the 148 SMs
-// where a per-image product of a small layer covers a fraction of them.
+// CUDA-core path for fp32 as the reference's default IEEE precision asks.  The patch rows are
+// padded to a multiple of 8 elements (and the weight copied with zero columns to match) so every
+// GEMM operand row is 16-byte aligned for TMA.
+//
+// Either way the output lands in NCHW directly (row k of image n's product is channel k of
+// image n), and one batched GEMM over many images fills the 148 SMs where a per-image product
+// of a small layer covers a fraction of them.
+#include "conv_gemm.h"
 #include "elementwise.cuh"
 
 namespace ntb {
@@ -24,7 +40,79 @@ struct ConvGeom {
   int sh, sw, ph, pw, dh, dw;
   int crs, crs_pad, pq_pad;
   int64_t xs[4];  // input strides (n, c, h, w) in elements
+  int implicit;   // implicit GEMM (im2col TMA loads) instead of a patch matrix
+  int cb, cs;     // implicit: 64-channel blocks per tap; channel extent of the [N, H, W, cs] map
+  int x_nhwc;     // implicit: the input already is channels-innermost with cs == C (no copy)
 };
+
+// Input [N, C, H, W] (any strides) -> [N, H, W, cs] contiguous, zero channels past C, for
+// 16-bit elements.  Block (wc, cc, nh) stages 64 channels x 64 columns of input row (n, h) in
+// shared memory (a warp reads a channel row's 64 columns as 32 element pairs when the rows are
+// unit-stride with even extents and strides, else element by element), then writes them out
+// pixel by pixel: a warp stores one pixel's 64 channels as 32 channel pairs, one 128-byte
+// segment per instruction.  The odd row pitch (65 elements) keeps the column reads of a warp on
+// distinct banks.  Grid z steps over (image, row).
+template <typename T>
+__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__ x, T* __restrict__ out, ConvGeom g,
+                                                           int64_t nh_total, int pairs) {
+  static_assert(sizeof(T) == 2, "16-bit elements");
+  constexpr int kC = 64, kW = 64, kPitch = kW + 1;
+  __shared__ T tile[kC * kPitch];
+  const int w0 = blockIdx.x * kW, c0 = blockIdx.y * kC;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t nh = blockIdx.z; nh < nh_total; nh += gridDim.z) {
+    const int64_t n = nh / g.H;
+    const int h = (int)(nh - n * g.H);
+    const T* xr = x + n * g.xs[0] + (int64_t)h * g.xs[2];
+    for (int ci = warp; ci < kC; ci += 8) {
+      const int c = c0 + ci;
+      const T* xc = xr + (int64_t)c * g.xs[1];
+      const int w = w0 + 2 * lane;
+      T v0 = cvt<T>(0.f), v1 = cvt<T>(0.f);
+      if (c < g.C) {
+        if (pairs) {
+          if (w < g.W) {  // W even: w + 1 < W too
+            const uint32_t u = *reinterpret_cast<const uint32_t*>(xc + w);
+            v0 = reinterpret_cast<const T*>(&u)[0];
+            v1 = reinterpret_cast<const T*>(&u)[1];
+          }
+        } else {
+          if (w < g.W) v0 = xc[(int64_t)w * g.xs[3]];
+          if (w + 1 < g.W) v1 = xc[(int64_t)(w + 1) * g.xs[3]];
+        }
+      }
+      tile[ci * kPitch + 2 * lane] = v0;
+      tile[ci * kPitch + 2 * lane + 1] = v1;
+    }
+    __syncthreads();
+    T* orow = out + nh * g.W * (int64_t)g.cs;
+    const int c = c0 + 2 * lane;
+    for (int wi = warp; wi < kW; wi += 8) {
+      const int w = w0 + wi;
+      if (w < g.W && c < g.cs) {
+        __align__(4) T pair[2] = {tile[(2 * lane) * kPitch + wi], tile[(2 * lane + 1) * kPitch + wi]};
+        *reinterpret_cast<uint32_t*>(orow + (int64_t)w * g.cs + c) = *reinterpret_cast<const uint32_t*>(pair);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Weight [K, C, R, S] (any strides) -> [K, R * S * cb * 64] contiguous: column
+// ((r * S + s) * cb + b) * 64 + i holds channel b * 64 + i of tap (r, s), zero past C.
+template <typename T>
+__global__ void __launch_bounds__(256) pack_weight_taps_kernel(const T* __restrict__ w, T* __restrict__ wp, ConvGeom g,
+                                                               int64_t ws0, int64_t ws1, int64_t ws2, int64_t ws3) {
+  const int per_tap = g.cb * 64;
+  const int64_t cols = (int64_t)g.R * g.S * per_tap;
+  const int64_t total = (int64_t)g.K * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(i / cols), col = (int)(i - (int64_t)k * cols);
+    const int rs = col / per_tap, c = col - rs * per_tap;
+    const int r = rs / g.S, s = rs - r * g.S;
+    wp[i] = c < g.C ? w[k * ws0 + c * ws1 + r * ws2 + s * ws3] : cvt<T>(0.f);
+  }
+}
 
 // Patch matrices of nb images: col[n] is [crs_pad, pq_pad] at col + n * crs_pad * pq_pad.
 // Block (x, row, n) writes 8 consecutive (p, q) columns per thread of patch row `row` of image
@@ -215,6 +303,10 @@ constexpr int64_t kColBudget = 1ll << 30;
 
 int64_t weight_bytes(const ConvGeom& g, int es) { return ((int64_t)g.K * g.crs_pad * es + 255) / 256 * 256; }
 int64_t image_bytes(const ConvGeom& g, int es) { return (int64_t)g.crs_pad * g.pq_pad * es; }
+int64_t tap_weight_bytes(const ConvGeom& g, int es) {
+  return ((int64_t)g.K * g.R * g.S * g.cb * 64 * es + 255) / 256 * 256;
+}
+int64_t nhwc_bytes(const ConvGeom& g, int64_t n, int es) { return n * g.H * g.W * g.cs * es; }
 
 int plan(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTensor* y, const int* prm,
          ConvGeom* g, int64_t* ws_bytes) {
@@ -257,11 +349,88 @@ int plan(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTe
     NTB_UNSUP(b->dtype == x->dtype, "bias dtype must equal the input dtype");
   }
   const int es = dtype_size(x->dtype);
+  // Implicit GEMM for 16-bit operands with at least 64 channels (fewer would pad the 64-channel
+  // blocks of the reduction with mostly zeros) inside the im2col map's limits.
+  g->cb = (g->C + 63) / 64;
+  g->cs = (g->C + 7) / 8 * 8;
+  g->x_nhwc = x->stride[1] == 1 && g->C % 8 == 0 && x->stride[3] == g->C && x->stride[2] == (int64_t)g->W * g->C &&
+              x->stride[0] % 8 == 0 && reinterpret_cast<uintptr_t>(x->data) % 16 == 0;
+  {
+    ConvImplicit cv{};
+    cv.dtype = x->dtype;
+    cv.x = cv.w = reinterpret_cast<const void*>(uintptr_t(256));  // placeholders: the run checks the real ones
+    cv.K = g->K;
+    cv.CB = g->cb;
+    cv.Cs = g->cs;
+    cv.H = g->H;
+    cv.W = g->W;
+    cv.N = (int)(x->shape[0] < (1 << 30) ? x->shape[0] : (1 << 30));
+    cv.R = g->R;
+    cv.S = g->S;
+    cv.P = g->P;
+    cv.Q = g->Q;
+    cv.sh = g->sh; cv.sw = g->sw; cv.ph = g->ph; cv.pw = g->pw; cv.dh = g->dh; cv.dw = g->dw;
+    g->implicit = g->C >= 64 && conv_implicit_ok(cv);
+  }
+  if (g->implicit) {
+    *ws_bytes = tap_weight_bytes(*g, es) + (g->x_nhwc ? 0 : nhwc_bytes(*g, x->shape[0], es));
+    return NTB_OK;
+  }
   const int64_t per = image_bytes(*g, es);
   int64_t nb = kColBudget / (per > 0 ? per : 1);
   nb = nb < 1 ? 1 : (nb > x->shape[0] ? x->shape[0] : nb);
   *ws_bytes = weight_bytes(*g, es) + (nb < 1 ? 1 : nb) * per;
   return NTB_OK;
+}
+
+// Implicit GEMM: packed weight, the input made channels-innermost (unless it already is), one
+// batched GEMM whose B tiles the TMA gathers from it window by window.
+template <typename T>
+int run_implicit(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTensor* y, const ConvGeom& g,
+                 uint8_t* ws, cudaStream_t st) {
+  const int es = sizeof(T);
+  const int64_t N = x->shape[0];
+  T* wp = reinterpret_cast<T*>(ws);
+  const int64_t wcount = (int64_t)g.K * g.R * g.S * g.cb * 64;
+  pack_weight_taps_kernel<T><<<grid_for(wcount), 256, 0, st>>>((const T*)w->data, wp, g, w->stride[0], w->stride[1],
+                                                                w->stride[2], w->stride[3]);
+  NTB_LAUNCH_CHECK();
+  ConvImplicit cv{};
+  cv.dtype = x->dtype;
+  cv.w = wp;
+  cv.K = g.K;
+  cv.CB = g.cb;
+  cv.Cs = g.cs;
+  cv.H = g.H;
+  cv.W = g.W;
+  cv.N = (int)N;
+  if (g.x_nhwc) {
+    cv.x = x->data;
+    cv.x_ns = x->stride[0];
+  } else {
+    T* xn = reinterpret_cast<T*>(ws + tap_weight_bytes(g, es));
+    const int64_t nh = N * g.H;
+    const unsigned gz = (unsigned)(nh < 65535 ? nh : 65535);
+    const int pairs = g.xs[3] == 1 && g.W % 2 == 0 && g.xs[2] % 2 == 0 && g.xs[1] % 2 == 0 && g.xs[0] % 2 == 0 &&
+                      reinterpret_cast<uintptr_t>(x->data) % 4 == 0;
+    nchw_to_nhwc_kernel<T><<<dim3((unsigned)((g.W + 63) / 64), (unsigned)((g.cs + 63) / 64), gz), 256, 0, st>>>(
+        (const T*)x->data, xn, g, nh, pairs);
+    NTB_LAUNCH_CHECK();
+    cv.x = xn;
+    cv.x_ns = (int64_t)g.H * g.W * g.cs;
+  }
+  cv.x_ws = g.cs;
+  cv.x_hs = (int64_t)g.W * g.cs;
+  cv.R = g.R;
+  cv.S = g.S;
+  cv.P = g.P;
+  cv.Q = g.Q;
+  cv.sh = g.sh; cv.sw = g.sw; cv.ph = g.ph; cv.pw = g.pw; cv.dh = g.dh; cv.dw = g.dw;
+  cv.y = y->data;
+  cv.y_ns = y->stride[0];
+  cv.bias = b != nullptr ? b->data : nullptr;
+  cv.bias_s = b != nullptr ? b->stride[0] : 0;
+  return conv_implicit_gemm(cv, st);
 }
 
 NtbTensor view3d(void* data, int dtype, int64_t n, int64_t rows, int64_t cols, int64_t ns, int64_t rs, int64_t cs) {
@@ -337,6 +506,14 @@ extern "C" int ntb_conv2d(const NtbTensor* x, const NtbTensor* w, const NtbTenso
   int rc = plan(x, w, b, y, params, &g, &need);
   if (rc != NTB_OK) return rc;
   if (x->shape[0] == 0 || g.K == 0) return NTB_OK;
+  if (g.implicit) {
+    NTB_ARG(workspace != nullptr && workspace_bytes >= need, "workspace too small: need %lld bytes", (long long)need);
+    NTB_ARG(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "workspace must be 256-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+    if (x->dtype == NTB_BF16) return run_implicit<__nv_bfloat16>(x, w, b, y, g, ws, st);
+    return run_implicit<__half>(x, w, b, y, g, ws, st);
+  }
   // Any workspace that holds the packed weight and one image's patch matrix works; more room
   // (up to the size ntb_conv2d_workspace reports) runs more images per batched GEMM.
   const int es = dtype_size(x->dtype);

@@ -28,6 +28,7 @@
 #include "elementwise.cuh"
 #include "sm100.cuh"
 #include "tma.cuh"
+#include "conv_gemm.h"
 
 namespace ntb {
 namespace gemm {
@@ -52,6 +53,9 @@ struct Params {
   int a_bcast, b_bcast;  // operand broadcast over the batch (batch stride 0): its tensor map holds
                          // one batch and every tile loads batch 0
   int band;        // M-blocks per raster band (power of two)
+  int b_im2col;    // B tiles are im2col loads of an [N, H, W, C] activation (implicit conv2d)
+  int cv_Q, cv_S, cv_cb;  // conv2d: output width, filter width, 64-channel blocks per filter tap
+  int cv_sh, cv_sw, cv_ph, cv_pw, cv_dh, cv_dw;
   void* d;
   int64_t d_bs, d_ms;  // output: batch and row strides (unit column stride)
   const void* c;       // optional addend (same dtype as d), any strides (0 = broadcast)
@@ -85,6 +89,31 @@ __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& b, i
   const int r = t - band * G * p.nblocks;
   mb = m0 + r % gm;
   nb = r / gm;
+}
+
+// im2col coordinates of an implicit-conv2d B tile: k-block kb is filter tap (r, s) =
+// divmod(kb / cv_cb, S) with channels (kb % cv_cb) * 64 ..; the tile's first column is output
+// pixel j = (j / Q, j % Q) of image b, whose window origin is (q * sw - pw, p * sh - ph).  The
+// load walks on from there through the image's later pixels (and into the next image: columns
+// past the image are computed and never stored); a tile starting past the image's last pixel
+// names image `batch`, which lies outside the map, and loads zeros.
+__device__ __forceinline__ void conv_coords(const Params& p, int kb, int b, int j, int& c, int& w, int& h, int& n,
+                                            uint16_t& off_w, uint16_t& off_h) {
+  const int rs = kb / p.cv_cb, cb = kb - rs * p.cv_cb;
+  const int r = rs / p.cv_S, s = rs - r * p.cv_S;
+  c = cb * 64;
+  off_w = (uint16_t)(s * p.cv_dw);
+  off_h = (uint16_t)(r * p.cv_dh);
+  if (j < p.N) {
+    const int pp = j / p.cv_Q, qq = j - pp * p.cv_Q;
+    w = qq * p.cv_sw - p.cv_pw;
+    h = pp * p.cv_sh - p.cv_ph;
+    n = b;
+  } else {
+    w = -p.cv_pw;
+    h = -p.cv_ph;
+    n = p.batch;
+  }
 }
 
 template <typename TD>
@@ -318,7 +347,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < BM / 64; ++j)
               sm100::tma_load_3d(a_dst + j * BK * kRowBytes, &tma_a, &full[stage], mb * BM + j * 64, kb * BK, ba);
           }
-          if (!p.b_mn) {
+          if (p.b_im2col) {
+            int c, w, h, n;
+            uint16_t ow, oh;
+            conv_coords(p, kb, b, nb * BN, c, w, h, n, ow, oh);
+            sm100::tma_load_im2col_4d(b_dst, &tma_b, &full[stage], c, w, h, n, ow, oh);
+          } else if (!p.b_mn) {
             sm100::tma_load_3d(b_dst, &tma_b, &full[stage], kb * BK, nb * BN, bb);
           } else {
 #pragma unroll
@@ -539,7 +573,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               sm100::tma_load_3d_pair_hint(a_dst + j * BK * kRowBytes, &tma_a, bar, row0 + j * 64, kb * BK, ba,
                                            pol_a);
           }
-          if (!p.b_mn) {
+          if (p.b_im2col) {
+            int c, w, h, n;
+            uint16_t ow, oh;
+            conv_coords(p, kb, b, col0, c, w, h, n, ow, oh);
+            sm100::tma_load_im2col_4d_pair(b_dst, &tma_b, bar, c, w, h, n, ow, oh);
+          } else if (!p.b_mn) {
             sm100::tma_load_3d_pair_hint(b_dst, &tma_b, bar, kb * BK, col0, bb, pol_b);
           } else {
 #pragma unroll
@@ -721,9 +760,19 @@ struct Operand {
   int64_t bs, s_outer, s_k;  // batch stride, stride along M (A) / N (B), stride along K
 };
 
+// B's tensor map of an implicit conv2d: im2col over the [N, H, W, Cs] activation, `pixels`
+// pixels of 64 channels per load.
+inline int encode_conv_b(CUtensorMap* tb, CUtensorMapDataType tdt, const ConvImplicit& cv, uint32_t pixels) {
+  const int64_t es = 2;
+  return tma::encode_im2col_4d(tb, tdt, const_cast<void*>(cv.x), (uint64_t)cv.Cs, (uint64_t)cv.W, (uint64_t)cv.H,
+                               (uint64_t)cv.N, (uint64_t)(cv.x_ws * es), (uint64_t)(cv.x_hs * es),
+                               (uint64_t)(cv.x_ns * es), -cv.pw, -cv.ph, cv.pw - (cv.S - 1) * cv.dw,
+                               cv.ph - (cv.R - 1) * cv.dh, 64, pixels, (uint32_t)cv.sw, (uint32_t)cv.sh);
+}
+
 template <typename T, typename TD, int BN, int STAGES, int EPI = kEpiPlain>
 int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& oa, const Operand& ob,
-              CUtensorMapDataType tdt, cudaStream_t st) {
+              CUtensorMapDataType tdt, cudaStream_t st, const ConvImplicit* cv = nullptr) {
   using S = Smem<BN, STAGES, sizeof(T)>;
   constexpr int BK = S::BK;
   const int es = sizeof(T);
@@ -738,7 +787,9 @@ int launch_tc(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& 
   else
     rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, BA, oa.s_k * es, (BA > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
   if (rc != NTB_OK) return rc;
-  if (!p.b_mn)
+  if (cv != nullptr)
+    rc = encode_conv_b(&tb, tdt, *cv, BN);
+  else if (!p.b_mn)
     rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, BB, ob.s_outer * es, (BB > 1 ? ob.bs : ob.s_outer * p.N) * es,
                         BK, BN);
   else
@@ -807,7 +858,7 @@ int pair_slots(int* slots) {
 
 template <typename T, typename TD, int STAGES, int EPI = kEpiPlain>
 int launch_tc_pair(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& oa, const Operand& ob,
-                   CUtensorMapDataType tdt, cudaStream_t st) {
+                   CUtensorMapDataType tdt, cudaStream_t st, const ConvImplicit* cv = nullptr) {
   using S = PairSmem<STAGES>;
   constexpr int BK = kRowBytes / 2;
   const int es = 2;
@@ -822,7 +873,9 @@ int launch_tc_pair(const NtbTensor* a, const NtbTensor* bm, Params p, const Oper
   else
     rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, BA, oa.s_k * es, (BA > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
   if (rc != NTB_OK) return rc;
-  if (!p.b_mn)
+  if (cv != nullptr)
+    rc = encode_conv_b(&tb, tdt, *cv, kPairBN / 2);
+  else if (!p.b_mn)
     rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, BB, ob.s_outer * es, (BB > 1 ? ob.bs : ob.s_outer * p.N) * es,
                         BK, kPairBN / 2);
   else
@@ -1156,3 +1209,77 @@ extern "C" int ntb_gemm_rope(const NtbTensor* a, const NtbTensor* w, const NtbTe
     return launch_tc_pair<__half, __half, 6, kEpiRope>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
   return launch_tc<__half, __half, 256, 4, kEpiRope>(a, w, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
 }
+
+namespace ntb {
+
+bool conv_implicit_ok(const ConvImplicit& cv) {
+  auto corner = [](int v) { return v >= -128 && v <= 127; };
+  return (cv.dtype == NTB_BF16 || cv.dtype == NTB_F16) && corner(-cv.pw) && corner(-cv.ph) &&
+         corner(cv.pw - (cv.S - 1) * cv.dw) && corner(cv.ph - (cv.R - 1) * cv.dh) && cv.sw <= 8 && cv.sh <= 8 &&
+         cv.Cs % 8 == 0 && reinterpret_cast<uintptr_t>(cv.x) % 16 == 0 && reinterpret_cast<uintptr_t>(cv.w) % 16 == 0 &&
+         (int64_t)cv.R * cv.S * cv.CB * 64 < (1ll << 31) && (int64_t)cv.P * cv.Q < (1ll << 31) && cv.N < (1 << 30);
+}
+
+int conv_implicit_gemm(const ConvImplicit& cv, cudaStream_t st) {
+  using namespace ntb::gemm;
+  NTB_ARG(conv_implicit_ok(cv), "convolution outside the im2col tensor map's limits");
+  Params p = {};
+  p.batch = cv.N;
+  p.M = cv.K;
+  p.N = cv.P * cv.Q;
+  p.K = cv.R * cv.S * cv.CB * 64;
+  p.d = cv.y;
+  p.d_bs = cv.y_ns;
+  p.d_ms = (int64_t)cv.P * cv.Q;
+  p.alpha = 1.f;
+  p.beta = cv.bias != nullptr ? 1.f : 0.f;
+  if (cv.bias != nullptr) {  // bias[k] broadcast over images and pixels
+    p.c = cv.bias;
+    p.c_bs = 0;
+    p.c_ms = cv.bias_s;
+    p.c_ns = 0;
+  }
+  p.err = device_error_ptr();
+  p.a_bcast = p.batch > 1;  // one weight for every image
+  p.b_im2col = 1;
+  p.cv_Q = cv.Q;
+  p.cv_S = cv.S;
+  p.cv_cb = cv.CB;
+  p.cv_sh = cv.sh;
+  p.cv_sw = cv.sw;
+  p.cv_ph = cv.ph;
+  p.cv_pw = cv.pw;
+  p.cv_dh = cv.dh;
+  p.cv_dw = cv.dw;
+  if ((int64_t)p.M * p.N * p.batch == 0) return NTB_OK;
+  NtbTensor a{};
+  a.data = const_cast<void*>(cv.w);
+  a.dtype = cv.dtype;
+  NtbTensor unused{};
+  const Operand oa{0, p.K, 1};
+  const Operand ob{0, 0, 1};
+  bool wide = p.N > 128;
+  if (wide) {  // as in ntb_gemm: the tile width with the better wave-quantised efficiency
+    const double sms = (double)sm_count();
+    const int64_t mb = (p.M + BM - 1) / BM;
+    const int64_t t256 = mb * ((p.N + 255) / 256) * p.batch, t128 = mb * ((p.N + 127) / 128) * p.batch;
+    const double e256 = (double)t256 / (std::ceil((double)t256 / sms) * sms);
+    const double e128 = 0.68 * (double)t128 / (std::ceil((double)t128 / sms) * sms);
+    wide = e256 >= e128;
+  }
+  if (cv.dtype == NTB_BF16) {
+    if (wide && use_pair(p))
+      return launch_tc_pair<__nv_bfloat16, __nv_bfloat16, 6>(&a, &unused, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                                             st, &cv);
+    return wide ? launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4>(&a, &unused, p, oa, ob,
+                                                                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st, &cv)
+                : launch_tc<__nv_bfloat16, __nv_bfloat16, 128, 6>(&a, &unused, p, oa, ob,
+                                                                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st, &cv);
+  }
+  if (wide && use_pair(p))
+    return launch_tc_pair<__half, __half, 6>(&a, &unused, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st, &cv);
+  return wide ? launch_tc<__half, __half, 256, 4>(&a, &unused, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st, &cv)
+              : launch_tc<__half, __half, 128, 6>(&a, &unused, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st, &cv);
+}
+
+}  // namespace ntb

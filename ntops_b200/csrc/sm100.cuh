@@ -205,6 +205,32 @@ __device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const void* tma
       : "memory");
 }
 
+// im2col-mode loads over a rank-4 (C, W, H, N) activation map (channels innermost): starting at
+// the window origin (w, h) of image n, the copy walks the map's pixel box (W fastest, then H,
+// then N, stepping by the map's element strides) for the map's pixels-per-column pixels and
+// writes, per pixel, the channels c .. c + channels-per-pixel - 1 of input pixel
+// (w + off_w, h + off_h) as one shared-memory row; pixels outside the input read zeros.  c must
+// keep c * element size a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_im2col_4d(void* smem_dst, const void* tmap, uint64_t* bar, int c, int w,
+                                                   int h, int n, uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)), "h"(off_w),
+      "h"(off_h)
+      : "memory");
+}
+// The same for a CTA pair running cta_group::2 MMAs (bytes complete on the leader's barrier).
+__device__ __forceinline__ void tma_load_im2col_4d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr,
+                                                        int c, int w, int h, int n, uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar_cluster_addr), "h"(off_w),
+      "h"(off_h)
+      : "memory");
+}
+
 // tma_load_3d_pair with an L2 cache policy (createpolicy): operands a raster keeps reused are
 // loaded evict-last, streamed ones evict-first.
 __device__ __forceinline__ void tma_load_3d_pair_hint(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr,

@@ -104,3 +104,46 @@ def test_conv2d_wide_rows_gather_path():
     b = torch.randn((3,), generator=g)
     got = nt.conv2d(x.to(DEV), wt.to(DEV), bias=b.to(DEV), stride=4, padding=2, dilation=3)
     assert_close(got, O.conv2d(x, wt, b, stride=4, padding=2, dilation=3), tol=(1e-5, 1e-5))
+
+
+# 16-bit convolutions with at least 64 input channels run as an implicit GEMM (TMA im2col loads
+# of the channels-innermost input): strides, dilations, asymmetric padding, a partial channel
+# block (96 = 64 + 32), output channels below / above one 128-row block and not a multiple of it,
+# 1x1 and 5x5 filters, one image, a partial last pixel tile.
+IMPLICIT_CASES = [
+    # n, c, h, w, k, (r, s), stride, padding, dilation
+    (2, 64, 28, 28, 128, (3, 3), 1, 1, 1),
+    (3, 96, 17, 23, 64, (3, 3), 2, (1, 2), 1),
+    (2, 64, 20, 20, 300, (3, 3), 1, 2, 2),
+    (1, 128, 14, 14, 256, (1, 1), 1, 0, 1),
+    (2, 64, 31, 29, 96, (5, 5), (2, 1), 2, (1, 2)),
+    (4, 256, 9, 9, 512, (3, 3), 1, 1, 1),
+    (2, 72, 12, 40, 40, (3, 1), (1, 3), (1, 0), (2, 1)),
+]
+
+
+@pytest.mark.parametrize("dtype", (torch.bfloat16, torch.float16))
+@pytest.mark.parametrize("case", IMPLICIT_CASES)
+def test_conv2d_implicit_gemm(case, dtype):
+    n, c, h, w, k, (r, s), stride, padding, dilation = case
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn((n, c, h, w), generator=g).to(dtype)
+    wt = (torch.randn((k, c, r, s), generator=g) * (1.0 / (c * r * s) ** 0.5)).to(dtype)
+    b = torch.randn((k,), generator=g).to(dtype)
+    got = nt.conv2d(x.to(DEV), wt.to(DEV), bias=b.to(DEV), stride=stride, padding=padding, dilation=dilation)
+    want = O.conv2d(x, wt, b, stride=stride, padding=padding, dilation=dilation)
+    assert got.shape == want.shape
+    assert_close(got, want, tol=(2e-2, 2e-2))
+
+
+def test_conv2d_implicit_channels_last_input():
+    """A channels-last input is read in place (no transposed copy) and matches the NCHW call."""
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn((3, 64, 15, 15), generator=g).to(torch.bfloat16)
+    wt = (torch.randn((128, 64, 3, 3), generator=g) * 0.05).to(torch.bfloat16)
+    xd = x.to(DEV)
+    xcl = xd.contiguous(memory_format=torch.channels_last)
+    got_cl = nt.conv2d(xcl, wt.to(DEV), padding=1)
+    got = nt.conv2d(xd, wt.to(DEV), padding=1)
+    assert torch.equal(got_cl, got)
+    assert_close(got, O.conv2d(x, wt, None, padding=1), tol=(2e-2, 2e-2))
