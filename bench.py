@@ -604,6 +604,10 @@ def run_case(name, reps):
         xc = torch.randn((32, 256, 56, 56), device=dev, generator=g).to(torch.bfloat16)
         wc = (torch.randn((256, 256, 3, 3), device=dev, generator=g) * 0.02).to(torch.bfloat16)
         fn = lambda: nt.conv2d(xc, wc, None, 1, 1)  # noqa: E731
+    elif name == "dropout":  # the per-op table's dropout line: p = 0.1 over 2^28 bf16 elements
+        g = torch.Generator(device=dev).manual_seed(0)
+        xdp = torch.randn(1 << 28, device=dev, generator=g).to(torch.bfloat16)
+        fn = lambda: nt.dropout(xdp, 0.1)  # noqa: E731
     elif name == "rope_q":
         from ntops_b200.chain import rope_tables
 

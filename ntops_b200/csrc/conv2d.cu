@@ -99,19 +99,19 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__
 }
 
 // Weight [K, C, R, S] (any strides) -> [K, R * S * cb * 64] contiguous: column
-// ((r * S + s) * cb + b) * 64 + i holds channel b * 64 + i of tap (r, s), zero past C.
+// ((r * S + s) * cb + b) * 64 + i holds channel b * 64 + i of tap (r, s), zero past C.  Block
+// (x, k) writes 256 consecutive columns of row k (32-bit index arithmetic only).
 template <typename T>
 __global__ void __launch_bounds__(256) pack_weight_taps_kernel(const T* __restrict__ w, T* __restrict__ wp, ConvGeom g,
                                                                int64_t ws0, int64_t ws1, int64_t ws2, int64_t ws3) {
   const int per_tap = g.cb * 64;
-  const int64_t cols = (int64_t)g.R * g.S * per_tap;
-  const int64_t total = (int64_t)g.K * cols;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int k = (int)(i / cols), col = (int)(i - (int64_t)k * cols);
-    const int rs = col / per_tap, c = col - rs * per_tap;
-    const int r = rs / g.S, s = rs - r * g.S;
-    wp[i] = c < g.C ? w[k * ws0 + c * ws1 + r * ws2 + s * ws3] : cvt<T>(0.f);
-  }
+  const int cols = g.R * g.S * per_tap;
+  const int k = blockIdx.y;
+  const int col = blockIdx.x * 256 + threadIdx.x;
+  if (col >= cols) return;
+  const int rs = col / per_tap, c = col - rs * per_tap;
+  const int r = rs / g.S, s = rs - r * g.S;
+  wp[(int64_t)k * cols + col] = c < g.C ? w[k * ws0 + c * ws1 + r * ws2 + s * ws3] : cvt<T>(0.f);
 }
 
 // Patch matrices of nb images: col[n] is [crs_pad, pq_pad] at col + n * crs_pad * pq_pad.
@@ -370,7 +370,7 @@ int plan(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, const NtbTe
     cv.P = g->P;
     cv.Q = g->Q;
     cv.sh = g->sh; cv.sw = g->sw; cv.ph = g->ph; cv.pw = g->pw; cv.dh = g->dh; cv.dw = g->dw;
-    g->implicit = g->C >= 64 && conv_implicit_ok(cv);
+    g->implicit = g->C >= 64 && g->K < 65536 && conv_implicit_ok(cv);
   }
   if (g->implicit) {
     *ws_bytes = tap_weight_bytes(*g, es) + (g->x_nhwc ? 0 : nhwc_bytes(*g, x->shape[0], es));
@@ -391,9 +391,9 @@ int run_implicit(const NtbTensor* x, const NtbTensor* w, const NtbTensor* b, con
   const int es = sizeof(T);
   const int64_t N = x->shape[0];
   T* wp = reinterpret_cast<T*>(ws);
-  const int64_t wcount = (int64_t)g.K * g.R * g.S * g.cb * 64;
-  pack_weight_taps_kernel<T><<<grid_for(wcount), 256, 0, st>>>((const T*)w->data, wp, g, w->stride[0], w->stride[1],
-                                                                w->stride[2], w->stride[3]);
+  const int cols = g.R * g.S * g.cb * 64;
+  pack_weight_taps_kernel<T><<<dim3((unsigned)((cols + 255) / 256), (unsigned)g.K), 256, 0, st>>>(
+      (const T*)w->data, wp, g, w->stride[0], w->stride[1], w->stride[2], w->stride[3]);
   NTB_LAUNCH_CHECK();
   ConvImplicit cv{};
   cv.dtype = x->dtype;
