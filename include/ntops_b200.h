@@ -253,6 +253,20 @@ NTB_API int ntb_conv2d(const NtbTensor* x, const NtbTensor* w, const NtbTensor* 
 NTB_API int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
              const NtbTensor* o, double scale, int causal_variant, void* stream);
 
+/* ntb_sdpa with a caller-provided workspace, which lets fp32 attention run on the tensor cores.
+ * The reference's fp32 attention multiplies with TF32 inputs (tl.dot's default precision for
+ * fp32); here fp32 q / k / v without a mask, with a positive scale and head_dim 64 / 128 are
+ * copied into the workspace as fp16 (the same 10-bit mantissa) with an exact power-of-two scale
+ * per tensor, the tcgen05 kernel runs on the copies and writes o in fp32 with the scales undone.
+ * ntb_sdpa_workspace() reports the bytes this path needs for these arguments (0 when the call
+ * takes another path, in which case ntb_sdpa_ws behaves as ntb_sdpa and ignores the
+ * workspace); the workspace must be 256-byte aligned.  Same reference as ntb_sdpa. */
+NTB_API int ntb_sdpa_workspace(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+                               const NtbTensor* o, double scale, int64_t* bytes);
+NTB_API int ntb_sdpa_ws(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+                        const NtbTensor* o, double scale, int causal_variant, void* workspace,
+                        int64_t workspace_bytes, void* stream);
+
 /* Attention for short query blocks (GQA group x Sq <= 64 rows per kv head, e.g. decoding
  * against a KV cache) split over the key range for parallelism.  Same tensors and semantics as
  * ntb_sdpa (fp16 / bf16 / fp32, head_dim <= 256, optional additive mask, causal variants);

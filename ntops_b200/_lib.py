@@ -63,6 +63,8 @@ EXPORTS = (
     "ntb_conv2d_workspace",
     "ntb_conv2d",
     "ntb_sdpa",
+    "ntb_sdpa_workspace",
+    "ntb_sdpa_ws",
     "ntb_sdpa_decode_workspace",
     "ntb_sdpa_decode",
     "ntb_sdpa_decode_static",
@@ -107,6 +109,8 @@ _SIGNATURES = {
     "ntb_conv2d": ([_P, _P, _P, _P, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _VP, ctypes.c_int64, _VP],
                    ctypes.c_int),
     "ntb_sdpa": ([_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP], ctypes.c_int),
+    "ntb_sdpa_workspace": ([_P, _P, _P, _P, _P, ctypes.c_double, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
+    "ntb_sdpa_ws": ([_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP, ctypes.c_int64, _VP], ctypes.c_int),
     "ntb_sdpa_decode_workspace": ([_P, _P, _P, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "ntb_sdpa_decode": (
         [_P, _P, _P, _P, _P, ctypes.c_double, ctypes.c_int, _VP, ctypes.c_int64, _VP],

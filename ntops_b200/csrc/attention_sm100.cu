@@ -75,7 +75,22 @@ struct Params {
   const void* mask;
   int64_t m_b, m_h, m_q;
   int mask_vec;
+  // fp32 attention staged to fp16 (see stage_max_kernel): the bit patterns of max|Q|, max|K|,
+  // max|V|, from which the kernel recovers the power-of-two scales the copies carry; NULL
+  // otherwise.
+  const unsigned int* stage_max;
 };
+
+// Exponent e of the staging scale 2^e for a tensor whose largest magnitude has the bit pattern
+// `bits`: the scaled maximum lies in [2^14, 2^15), inside fp16's range with its full 11-bit
+// precision for the largest elements; 0 for an all-zero or non-finite tensor.
+__host__ __device__ __forceinline__ int stage_exp(unsigned int bits) {
+  const int biased = (int)((bits >> 23) & 0xFFu);
+  if (bits == 0u || biased == 0xFF) return 0;
+  const int E = biased == 0 ? -126 : biased - 126;  // max < 2^E (subnormal maxima: 2^-126)
+  const int e = 15 - E;
+  return e < -110 ? -110 : (e > 110 ? 110 : e);
+}
 
 template <int D>
 struct Smem {
@@ -199,11 +214,24 @@ __device__ __forceinline__ void load_mask_row(const T* mrow, int k0, int skv, bo
   }
 }
 
-template <typename T, int D, bool MASK>
+// TO: output type (T, or float for fp32 attention staged to fp16).
+template <typename T, int D, bool MASK, typename TO = T>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, Params p) {
   using S = Smem<D>;
+  // Staged fp32 inputs carry scales 2^eq, 2^ek, 2^ev: the scores come out 2^(eq + ek) too large
+  // and O 2^ev too large; both are undone exactly here.
+  // (Only the staged instantiation, whose output type differs from its operand type, reads
+  // them; the others compile exactly as without staging.)
+  float scale_log2 = p.scale_log2, out_mul = 1.f;
+  if constexpr (!std::is_same<TO, T>::value) {
+    if (p.stage_max != nullptr) {
+      const int eq = stage_exp(p.stage_max[0]), ek = stage_exp(p.stage_max[1]), ev = stage_exp(p.stage_max[2]);
+      scale_log2 = ldexpf(p.scale_log2, -(eq + ek));
+      out_mul = ldexpf(1.f, -ev);
+    }
+  }
   constexpr uint32_t kFormat = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t TMEM_COLS = 512;
 
@@ -433,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) {
             const uint32_t w = mk[c * 16 + (i >> 1)];
             const float mv = widen16<T>((i & 1) ? (w >> 16) : (w & 0xFFFFu));
-            sr[c][i] = __float_as_uint(fmaf(__uint_as_float(sr[c][i]), p.scale_log2, mv * kLog2e));
+            sr[c][i] = __float_as_uint(fmaf(__uint_as_float(sr[c][i]), scale_log2, mv * kLog2e));
           }
         }
       }
@@ -456,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
       // (unmasked: the max of S times the scale, which the host only allows to be positive)
-      const float m_blk = MASK ? mx : mx * p.scale_log2;
+      const float m_blk = MASK ? mx : mx * scale_log2;
       // Rescale O and l only when the max grows by more than the threshold (done after P is
       // written, before P is published: PV_t(j) must accumulate into the rescaled O).
       const bool grow = m_blk > m_used + kRescaleThreshold;
@@ -466,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = exp2(S * scale_log2 - m) as packed 16-bit pairs over S's first 64 columns, the
       // argument in packed fp32x2; the fp32 probabilities stay in sr for the row sum, which is
       // taken after P is published (off the path to the next MMA)
-      const float2 sc2 = MASK ? make_float2(1.f, 1.f) : make_float2(p.scale_log2, p.scale_log2);
+      const float2 sc2 = MASK ? make_float2(1.f, 1.f) : make_float2(scale_log2, scale_log2);
       const float2 nm2 = make_float2(-m_ref, -m_ref);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -520,8 +548,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = sm100::mbar_wait(&pv_done[t], (uint32_t)((nkv_mine - 1) & 1), abort_flag, p.err);
     sm100::tc_fence_after();
     if (ok) {
-      const float inv = 1.f / l;  // l == 0 (fully masked row) gives NaN, as torch does
-      T* orow = reinterpret_cast<T*>(p.o) + (int64_t)b * p.o_b + (int64_t)hq * p.o_h + (int64_t)row * p.o_s;
+      const float inv = out_mul / l;  // l == 0 (fully masked row) gives NaN, as torch does
+      TO* orow = reinterpret_cast<TO*>(p.o) + (int64_t)b * p.o_b + (int64_t)hq * p.o_h + (int64_t)row * p.o_s;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
@@ -534,11 +562,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (row < p.Sq) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            ew::Vec<T, 8> v;
+          for (int i = 0; i < 32; i += 16 / (int)sizeof(TO)) {
+            constexpr int V = 16 / sizeof(TO);  // one 16-byte store
+            ew::Vec<TO, V> v;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v.v[e] = cvt<T>(__uint_as_float(r[i + e]) * inv);
-            *reinterpret_cast<ew::Vec<T, 8>*>(orow + c * 32 + i) = v;
+            for (int e = 0; e < V; ++e) v.v[e] = cvt<TO>(__uint_as_float(r[i + e]) * inv);
+            *reinterpret_cast<ew::Vec<TO, V>*>(orow + c * 32 + i) = v;
           }
         }
       }
@@ -651,8 +680,64 @@ __global__ void __launch_bounds__(128) attn_generic_kernel(GenArgs a, Params p) 
   }
 }
 
+// ------------------------------------------------------------- fp32 staging -------------
+// fp32 attention on the tensor cores.  The reference's fp32 attention multiplies through tl.dot,
+// whose default input precision for fp32 operands is TF32 (10-bit mantissa).  Here Q, K and V
+// are copied to fp16 (the same 10-bit mantissa) with an exact power-of-two scale per tensor that
+// puts the tensor's largest magnitude in [2^14, 2^15) (so fp16's range costs no precision for
+// the large elements), the fp16 tcgen05 kernel runs on the copies, and the scales are undone
+// exactly: the softmax scale takes 2^-(eq + ek), the output 2^-ev, written in fp32.
+struct StageT {
+  const float* src;
+  __half* dst;              // dense [B, H, S, D]
+  int64_t sb, sh, ss, sd;   // source strides in elements
+  int H, S, D;
+  int64_t rows;             // B * H * S
+};
+struct StageSet {
+  StageT t[3];  // Q, K, V (blockIdx.y)
+};
+
+// max |x| of each tensor as float bits (non-negative floats order like their bit patterns);
+// one warp per row, rows grid-strided.
+__global__ void __launch_bounds__(256) stage_max_kernel(StageSet set, unsigned int* maxbits) {
+  const StageT& a = set.t[blockIdx.y];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float m = 0.f;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.rows; row += (int64_t)gridDim.x * 8) {
+    const int64_t bh = row / a.S, si = row - bh * a.S;
+    const int64_t b = bh / a.H, h = bh - b * a.H;
+    const float* x = a.src + b * a.sb + h * a.sh + si * a.ss;
+    for (int d = lane; d < a.D; d += 32) m = fmaxf(m, fabsf(x[d * a.sd]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0 && m > 0.f) atomicMax(&maxbits[blockIdx.y], __float_as_uint(m));
+}
+
+__global__ void __launch_bounds__(256) stage_convert_kernel(StageSet set, const unsigned int* maxbits) {
+  const StageT& a = set.t[blockIdx.y];
+  const int e = stage_exp(maxbits[blockIdx.y]);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.rows; row += (int64_t)gridDim.x * 8) {
+    const int64_t bh = row / a.S, si = row - bh * a.S;
+    const int64_t b = bh / a.H, h = bh - b * a.H;
+    const float* x = a.src + b * a.sb + h * a.sh + si * a.ss;
+    __half* y = a.dst + row * a.D;
+    for (int d = lane; d < a.D; d += 32) y[d] = __float2half_rn(ldexpf(x[d * a.sd], e));
+  }
+}
+
+// Workspace of the staged fp32 path: 256 B of maxima, then the fp16 copies of Q, K, V.
+int64_t stage_bytes(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v) {
+  auto dense = [](const NtbTensor* t) {
+    return ((int64_t)t->shape[0] * t->shape[1] * t->shape[2] * t->shape[3] * 2 + 255) / 256 * 256;
+  };
+  return 256 + dense(q) + dense(k) + dense(v);
+}
+
 // ---------------------------------------------------------------------------- host -------
-template <typename T, int D, bool MASK>
+template <typename T, int D, bool MASK, typename TO = T>
 int launch_tc(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, Params p, CUtensorMapDataType tdt,
               cudaStream_t st) {
   using S = Smem<D>;
@@ -675,7 +760,7 @@ int launch_tc(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, Params
   if ((rc = tma::encode_4d(&tv, tdt, v->data, p.D, p.Skv, p.Hkv, p.B, sb(v, 2), sb(v, 1), sb(v, 0), 64, BLK)) !=
       NTB_OK)
     return rc;
-  auto kernel = attn_tc_kernel<T, D, MASK>;
+  auto kernel = attn_tc_kernel<T, D, MASK, TO>;
   {
     // The register split assumes the compiled launch register count (kLaunchRegs).
     static std::atomic<int> regs_ok{0};
@@ -739,10 +824,27 @@ bool tma_attn_ok(const NtbTensor* t, int es) {
 }  // namespace attn
 }  // namespace ntb
 
-extern "C" int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
-                        const NtbTensor* o, double scale, int causal_variant, void* stream) {
-  using namespace ntb;
-  using namespace ntb::attn;
+namespace ntb {
+namespace attn {
+namespace {
+
+// fp32 q / k / v / out, no mask, positive scale, head_dim 64 / 128, an output the fp32 epilogue
+// can store with 16-byte vectors: the staged tensor-core path applies.
+bool staged_ok(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+               const NtbTensor* o, double scale) {
+  if (q->dtype != NTB_F32 || k->dtype != NTB_F32 || v->dtype != NTB_F32 || o->dtype != NTB_F32) return false;
+  if (mask != nullptr || !(scale > 0.0)) return false;
+  const int64_t D = q->shape[3];
+  if (!(D == 64 || D == 128) || v->shape[3] != D || k->shape[2] <= 0) return false;
+  if (reinterpret_cast<uintptr_t>(o->data) % 16 != 0 || o->stride[3] != 1) return false;
+  if (o->stride[2] % 4 != 0 || (o->stride[1] % 4 != 0 && o->shape[1] > 1) || (o->stride[0] % 4 != 0 && o->shape[0] > 1))
+    return false;
+  return true;
+}
+
+int sdpa_impl(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+              const NtbTensor* o, double scale, int causal_variant, void* workspace, int64_t workspace_bytes,
+              void* stream) {
   int rc;
   if ((rc = check_tensor(q, "query")) != NTB_OK) return rc;
   if ((rc = check_tensor(k, "key")) != NTB_OK) return rc;
@@ -822,6 +924,86 @@ extern "C" int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor*
     return p.D == 128 ? launch_tc<__half, 128, false>(q, k, v, p, tdt, st)
                       : launch_tc<__half, 64, false>(q, k, v, p, tdt, st);
   }
+  if (workspace != nullptr && staged_ok(q, k, v, mask, o, scale)) {
+    NTB_ARG(workspace_bytes >= stage_bytes(q, k, v) && reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+            "attention workspace too small or not 256-byte aligned (need %lld bytes)",
+            (long long)stage_bytes(q, k, v));
+    uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+    unsigned int* maxbits = reinterpret_cast<unsigned int*>(ws);
+    NtbTensor st16[3];
+    StageSet set;
+    const NtbTensor* src[3] = {q, k, v};
+    uint8_t* cur = ws + 256;
+    int64_t max_rows = 0;
+    for (int i = 0; i < 3; ++i) {
+      const NtbTensor* t = src[i];
+      NtbTensor d{};
+      d.data = cur;
+      d.dtype = NTB_F16;
+      d.ndim = 4;
+      for (int j = 0; j < 4; ++j) d.shape[j] = t->shape[j];
+      d.stride[3] = 1;
+      d.stride[2] = t->shape[3];
+      d.stride[1] = t->shape[2] * t->shape[3];
+      d.stride[0] = t->shape[1] * d.stride[1];
+      st16[i] = d;
+      StageT& a = set.t[i];
+      a.src = reinterpret_cast<const float*>(t->data);
+      a.dst = reinterpret_cast<__half*>(cur);
+      a.sb = t->stride[0];
+      a.sh = t->stride[1];
+      a.ss = t->stride[2];
+      a.sd = t->stride[3];
+      a.H = (int)t->shape[1];
+      a.S = (int)t->shape[2];
+      a.D = (int)t->shape[3];
+      a.rows = t->shape[0] * t->shape[1] * t->shape[2];
+      if (a.rows > max_rows) max_rows = a.rows;
+      cur += (t->shape[0] * t->shape[1] * t->shape[2] * t->shape[3] * 2 + 255) / 256 * 256;
+    }
+    NTB_CUDA(cudaMemsetAsync(maxbits, 0, 3 * sizeof(unsigned int), st));
+    int64_t gx = (max_rows + 7) / 8;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    if (gx > cap) gx = cap;
+    stage_max_kernel<<<dim3((unsigned)gx, 3), 256, 0, st>>>(set, maxbits);
+    NTB_LAUNCH_CHECK();
+    stage_convert_kernel<<<dim3((unsigned)gx, 3), 256, 0, st>>>(set, maxbits);
+    NTB_LAUNCH_CHECK();
+    p.stage_max = maxbits;
+    const CUtensorMapDataType tdt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    return p.D == 128 ? launch_tc<__half, 128, false, float>(&st16[0], &st16[1], &st16[2], p, tdt, st)
+                      : launch_tc<__half, 64, false, float>(&st16[0], &st16[1], &st16[2], p, tdt, st);
+  }
   NTB_DISPATCH_FLOAT(q->dtype, return launch_generic<scalar_t>(q, k, v, mask, p, (int)v->shape[3], st));
   return NTB_OK;
+}
+
+}  // namespace
+}  // namespace attn
+}  // namespace ntb
+
+extern "C" int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+                        const NtbTensor* o, double scale, int causal_variant, void* stream) {
+  return ntb::attn::sdpa_impl(q, k, v, mask, o, scale, causal_variant, nullptr, 0, stream);
+}
+
+extern "C" int ntb_sdpa_workspace(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+                                  const NtbTensor* o, double scale, int64_t* bytes) {
+  using namespace ntb;
+  using namespace ntb::attn;
+  NTB_ARG(bytes != nullptr, "bytes is NULL");
+  int rc;
+  if ((rc = check_tensor(q, "query")) != NTB_OK) return rc;
+  if ((rc = check_tensor(k, "key")) != NTB_OK) return rc;
+  if ((rc = check_tensor(v, "value")) != NTB_OK) return rc;
+  if ((rc = check_tensor(o, "output")) != NTB_OK) return rc;
+  NTB_ARG(q->ndim == 4 && k->ndim == 4 && v->ndim == 4 && o->ndim == 4, "q, k, v, out must be 4-D [B, H, S, D]");
+  *bytes = staged_ok(q, k, v, mask, o, scale) ? stage_bytes(q, k, v) : 0;
+  return NTB_OK;
+}
+
+extern "C" int ntb_sdpa_ws(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
+                           const NtbTensor* o, double scale, int causal_variant, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
+  return ntb::attn::sdpa_impl(q, k, v, mask, o, scale, causal_variant, workspace, workspace_bytes, stream);
 }

@@ -102,6 +102,19 @@ def scaled_dot_product_attention(
                ctypes.byref(vd), _lib.ref(md), ctypes.byref(od), float(scale), causal,
                ctypes.c_void_p(ws.data_ptr()), nbytes.value, device_tensor=output)
         return output
+    if q.dtype == torch.float32:
+        # fp32 runs on the tensor cores through fp16 copies in a workspace (TF32-equivalent
+        # precision, as the reference's tl.dot on fp32); 0 bytes when the call takes another path.
+        nbytes = ctypes.c_int64(0)
+        _lib.check(lib().ntb_sdpa_workspace(ctypes.byref(qd), ctypes.byref(kd), ctypes.byref(vd), _lib.ref(md),
+                                            ctypes.byref(od), float(scale), ctypes.byref(nbytes)),
+                   "scaled_dot_product_attention")
+        if nbytes.value > 0:
+            ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device)
+            launch("scaled_dot_product_attention", lib().ntb_sdpa_ws, ctypes.byref(qd), ctypes.byref(kd),
+                   ctypes.byref(vd), _lib.ref(md), ctypes.byref(od), float(scale), causal,
+                   ctypes.c_void_p(ws.data_ptr()), nbytes.value, device_tensor=output)
+            return output
     launch("scaled_dot_product_attention", lib().ntb_sdpa, ctypes.byref(qd), ctypes.byref(kd),
            ctypes.byref(vd), _lib.ref(md), ctypes.byref(od), float(scale), causal, device_tensor=output)
     return output

@@ -180,3 +180,71 @@ def test_negative_scale_without_mask(dtype):
     q, k, v = (torch.randn((1, 2, 256, 128), generator=g).to(dtype) for _ in range(3))
     got = nt.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV), scale=-0.05)
     assert_close(got, O.scaled_dot_product_attention(q, k, v, None, False, -0.05), tol=(2.5e-2, 2.5e-2))
+
+
+# fp32 attention on the tensor cores (fp16 copies with an exact power-of-two scale per tensor,
+# TF32-equivalent precision like the reference's tl.dot on fp32): magnitudes far from 1 in both
+# directions, head_dim 64 / 128, causal variants, GQA, Sq != Skv, strided [B, S, H, D] views.
+FP32_TC_CASES = [
+    # b, hq, hkv, sq, skv, d, magnitude, causal, layout
+    (1, 4, 2, 1024, 1024, 128, 1.0, None, "bhsd"),
+    (2, 8, 2, 300, 517, 64, 1e3, None, "bhsd"),
+    (1, 4, 4, 777, 777, 128, 1e-3, CausalVariant.UPPER_LEFT, "bhsd"),
+    (2, 4, 1, 200, 640, 64, 37.0, CausalVariant.LOWER_RIGHT, "bshd"),
+    (1, 2, 2, 2048, 2048, 128, 0.05, CausalVariant.UPPER_LEFT, "bshd"),
+]
+
+
+@pytest.mark.parametrize("case", FP32_TC_CASES)
+def test_fp32_tensor_core_staged(case):
+    b, hq, hkv, sq, skv, d, mag, causal, layout = case
+    g = torch.Generator().manual_seed(11)
+    q = torch.randn((b, hq, sq, d), generator=g) * mag
+    k = torch.randn((b, hkv, skv, d), generator=g) * mag
+    v = torch.randn((b, hkv, skv, d), generator=g) * mag
+    scale = 1.0 / (math.sqrt(d) * mag * mag) if mag != 1.0 else None
+    if layout == "bshd":
+        qd, kd, vd = (t.transpose(1, 2).contiguous().to(DEV).transpose(1, 2) for t in (q, k, v))
+    else:
+        qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    kw = {}
+    if causal is None:
+        want = O.scaled_dot_product_attention(q, k, v, None, False, scale)
+    else:
+        kw = {"is_causal": True, "causal_variant": causal}
+        want = O.scaled_dot_product_attention(q, k, v, None, True, scale, causal_variant=int(causal))
+    got = nt.scaled_dot_product_attention(qd, kd, vd, scale=scale, enable_gqa=True, **kw)
+    assert got.dtype == torch.float32
+    assert_close(got, want, tol=(1e-2, 1e-2 * mag))
+
+
+def test_fp32_workspace_query():
+    """The staged path asks for a workspace only for fp32 without a mask and with a positive
+    scale; ntb_sdpa (no workspace) still runs fp32 on the CUDA-core kernel, within the same
+    tolerance of the oracle."""
+    import ctypes
+
+    from ntops_b200 import _lib as L
+
+    lib = L.load()
+    g = torch.Generator().manual_seed(12)
+    q, k, v = (torch.randn((1, 2, 256, 64), generator=g) for _ in range(3))
+    o = torch.empty((1, 2, 256, 64), device=DEV)
+    qg, kg, vg = q.to(DEV), k.to(DEV), v.to(DEV)  # kept alive while their descriptors are used
+    qd, kd, vd, od = (L.describe(t) for t in (qg, kg, vg, o))
+    nbytes = ctypes.c_int64(-1)
+    assert lib.ntb_sdpa_workspace(ctypes.byref(qd), ctypes.byref(kd), ctypes.byref(vd), None, ctypes.byref(od),
+                                  0.125, ctypes.byref(nbytes)) == L.OK
+    assert nbytes.value >= 256 + 3 * 256 * 64 * 2 * 2
+    assert lib.ntb_sdpa_workspace(ctypes.byref(qd), ctypes.byref(kd), ctypes.byref(vd), None, ctypes.byref(od),
+                                  -0.125, ctypes.byref(nbytes)) == L.OK
+    assert nbytes.value == 0
+    qb, kb, vb, ob = (t.to(DEV, torch.bfloat16) for t in (q, k, v, o))
+    qbd, kbd, vbd, obd = (L.describe(t) for t in (qb, kb, vb, ob))
+    assert lib.ntb_sdpa_workspace(ctypes.byref(qbd), ctypes.byref(kbd), ctypes.byref(vbd), None,
+                                  ctypes.byref(obd), 0.125, ctypes.byref(nbytes)) == L.OK
+    assert nbytes.value == 0
+    assert lib.ntb_sdpa(ctypes.byref(qd), ctypes.byref(kd), ctypes.byref(vd), None, ctypes.byref(od), 0.125, 0,
+                        None) == L.OK
+    torch.cuda.synchronize()
+    assert_close(o.cpu(), O.scaled_dot_product_attention(q, k, v, None, False, 0.125), tol=(1e-2, 1e-2))
