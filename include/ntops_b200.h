@@ -255,9 +255,11 @@ NTB_API int ntb_sdpa(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v,
 
 /* ntb_sdpa with a caller-provided workspace, which lets fp32 attention run on the tensor cores.
  * The reference's fp32 attention multiplies with TF32 inputs (tl.dot's default precision for
- * fp32); here fp32 q / k / v without a mask, with a positive scale and head_dim 64 / 128 are
- * copied into the workspace as fp16 (the same 10-bit mantissa) with an exact power-of-two scale
- * per tensor, the tcgen05 kernel runs on the copies and writes o in fp32 with the scales undone.
+ * fp32); here fp32 q / k / v with head_dim 64 / 128 (and a positive scale when there is no
+ * mask) are copied into the workspace as fp16 (the same 10-bit mantissa) with an exact
+ * power-of-two scale per tensor, an fp32 mask as fp16 in its broadcast shape (values beyond
+ * fp16's range become +-inf), the tcgen05 kernel runs on the copies and writes o in fp32 with
+ * the scales undone.
  * ntb_sdpa_workspace() reports the bytes this path needs for these arguments (0 when the call
  * takes another path, in which case ntb_sdpa_ws behaves as ntb_sdpa and ignores the
  * workspace); the workspace must be 256-byte aligned.  Same reference as ntb_sdpa. */

@@ -728,12 +728,46 @@ __global__ void __launch_bounds__(256) stage_convert_kernel(StageSet set, const 
   }
 }
 
-// Workspace of the staged fp32 path: 256 B of maxima, then the fp16 copies of Q, K, V.
-int64_t stage_bytes(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v) {
+// Additive mask of the staged path: fp16 copy [Bm, Hm, Qm, Skv8] of the mask in its broadcast
+// shape (a dimension of stride 0 kept at extent 1), rows padded with zeros to a multiple of 8
+// keys (16-byte aligned row segments).  Values beyond fp16's range become +-inf (-inf masks a
+// key, as a huge negative logit does).
+struct StageMask {
+  const float* src;
+  __half* dst;
+  int64_t sb, sh, sq, sk;  // source strides (0 for a broadcast dimension)
+  int Hm, Qm, Skv, Skv8;
+  int64_t rows;            // Bm * Hm * Qm
+};
+
+__global__ void __launch_bounds__(256) stage_mask_kernel(StageMask a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.rows; row += (int64_t)gridDim.x * 8) {
+    const int64_t bh = row / a.Qm, qi = row - bh * a.Qm;
+    const int64_t b = bh / a.Hm, h = bh - b * a.Hm;
+    const float* m = a.src + b * a.sb + h * a.sh + qi * a.sq;
+    __half* y = a.dst + row * a.Skv8;
+    for (int j = lane; j < a.Skv8; j += 32) y[j] = j < a.Skv ? __float2half_rn(m[j * a.sk]) : __float2half_rn(0.f);
+  }
+}
+
+// Broadcast extents of a mask (1 where the stride is 0 or the extent is 1).
+inline void mask_extents(const NtbTensor* m, int64_t ext[3]) {
+  for (int i = 0; i < 3; ++i) ext[i] = (m->shape[i] == 1 || m->stride[i] == 0) ? 1 : m->shape[i];
+}
+
+// Workspace of the staged fp32 path: 256 B of maxima, the fp16 copies of Q, K, V, and the mask's.
+int64_t stage_bytes(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask) {
   auto dense = [](const NtbTensor* t) {
     return ((int64_t)t->shape[0] * t->shape[1] * t->shape[2] * t->shape[3] * 2 + 255) / 256 * 256;
   };
-  return 256 + dense(q) + dense(k) + dense(v);
+  int64_t bytes = 256 + dense(q) + dense(k) + dense(v);
+  if (mask != nullptr) {
+    int64_t ext[3];
+    mask_extents(mask, ext);
+    bytes += (ext[0] * ext[1] * ext[2] * ((mask->shape[3] + 7) / 8 * 8) * 2 + 255) / 256 * 256;
+  }
+  return bytes;
 }
 
 // ---------------------------------------------------------------------------- host -------
@@ -828,12 +862,13 @@ namespace ntb {
 namespace attn {
 namespace {
 
-// fp32 q / k / v / out, no mask, positive scale, head_dim 64 / 128, an output the fp32 epilogue
-// can store with 16-byte vectors: the staged tensor-core path applies.
+// fp32 q / k / v / out (and mask), head_dim 64 / 128, a positive scale without a mask (the
+// unmasked kernel scales the raw scores' max), an output the fp32 epilogue can store with
+// 16-byte vectors: the staged tensor-core path applies.
 bool staged_ok(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const NtbTensor* mask,
                const NtbTensor* o, double scale) {
   if (q->dtype != NTB_F32 || k->dtype != NTB_F32 || v->dtype != NTB_F32 || o->dtype != NTB_F32) return false;
-  if (mask != nullptr || !(scale > 0.0)) return false;
+  if (mask != nullptr ? mask->dtype != NTB_F32 || mask->ndim != 4 : !(scale > 0.0)) return false;
   const int64_t D = q->shape[3];
   if (!(D == 64 || D == 128) || v->shape[3] != D || k->shape[2] <= 0) return false;
   if (reinterpret_cast<uintptr_t>(o->data) % 16 != 0 || o->stride[3] != 1) return false;
@@ -925,9 +960,9 @@ int sdpa_impl(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const 
                       : launch_tc<__half, 64, false>(q, k, v, p, tdt, st);
   }
   if (workspace != nullptr && staged_ok(q, k, v, mask, o, scale)) {
-    NTB_ARG(workspace_bytes >= stage_bytes(q, k, v) && reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+    NTB_ARG(workspace_bytes >= stage_bytes(q, k, v, mask) && reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
             "attention workspace too small or not 256-byte aligned (need %lld bytes)",
-            (long long)stage_bytes(q, k, v));
+            (long long)stage_bytes(q, k, v, mask));
     uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
     unsigned int* maxbits = reinterpret_cast<unsigned int*>(ws);
     NtbTensor st16[3];
@@ -971,6 +1006,33 @@ int sdpa_impl(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const 
     NTB_LAUNCH_CHECK();
     p.stage_max = maxbits;
     const CUtensorMapDataType tdt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (mask != nullptr) {
+      int64_t ext[3];
+      mask_extents(mask, ext);
+      StageMask sm;
+      sm.src = reinterpret_cast<const float*>(mask->data);
+      sm.dst = reinterpret_cast<__half*>(cur);
+      sm.sb = ext[0] > 1 ? mask->stride[0] : 0;
+      sm.sh = ext[1] > 1 ? mask->stride[1] : 0;
+      sm.sq = ext[2] > 1 ? mask->stride[2] : 0;
+      sm.sk = mask->stride[3];
+      sm.Hm = (int)ext[1];
+      sm.Qm = (int)ext[2];
+      sm.Skv = (int)mask->shape[3];
+      sm.Skv8 = (sm.Skv + 7) / 8 * 8;
+      sm.rows = ext[0] * ext[1] * ext[2];
+      int64_t mx = (sm.rows + 7) / 8;
+      if (mx > cap) mx = cap;
+      stage_mask_kernel<<<(unsigned)mx, 256, 0, st>>>(sm);
+      NTB_LAUNCH_CHECK();
+      p.mask = cur;
+      p.m_b = ext[0] > 1 ? ext[1] * ext[2] * sm.Skv8 : 0;
+      p.m_h = ext[1] > 1 ? ext[2] * sm.Skv8 : 0;
+      p.m_q = ext[2] > 1 ? sm.Skv8 : 0;
+      p.mask_vec = 1;
+      return p.D == 128 ? launch_tc<__half, 128, true, float>(&st16[0], &st16[1], &st16[2], p, tdt, st)
+                        : launch_tc<__half, 64, true, float>(&st16[0], &st16[1], &st16[2], p, tdt, st);
+    }
     return p.D == 128 ? launch_tc<__half, 128, false, float>(&st16[0], &st16[1], &st16[2], p, tdt, st)
                       : launch_tc<__half, 64, false, float>(&st16[0], &st16[1], &st16[2], p, tdt, st);
   }
@@ -998,7 +1060,8 @@ extern "C" int ntb_sdpa_workspace(const NtbTensor* q, const NtbTensor* k, const 
   if ((rc = check_tensor(v, "value")) != NTB_OK) return rc;
   if ((rc = check_tensor(o, "output")) != NTB_OK) return rc;
   NTB_ARG(q->ndim == 4 && k->ndim == 4 && v->ndim == 4 && o->ndim == 4, "q, k, v, out must be 4-D [B, H, S, D]");
-  *bytes = staged_ok(q, k, v, mask, o, scale) ? stage_bytes(q, k, v) : 0;
+  if (mask != nullptr && (rc = check_tensor(mask, "attn_mask")) != NTB_OK) return rc;
+  *bytes = staged_ok(q, k, v, mask, o, scale) ? stage_bytes(q, k, v, mask) : 0;
   return NTB_OK;
 }
 
