@@ -421,6 +421,13 @@ def per_op_table(dev, peaks, with_cpu=True):
        fl * (8192 + 1) / (2 * 8192),
        cpu=(lambda: F.scaled_dot_product_attention(qac, kac, vac, is_causal=True), note, 256.0))
     del qa, ka, va, qac, kac, vac
+    # fp32 attention (not a BASELINE config; C5's shape with batch 2): tensor cores through fp16
+    # copies in a workspace, staging included in the time
+    qf, kf, vf = (torch.randn(2, 32, 8192, 128, generator=g, device=dev) for _ in range(3))
+    qfc, kfc, vfc = (qf[:1, :1].cpu(), kf[:1, :1].cpu(), vf[:1, :1].cpu()) if with_cpu else (None,) * 3
+    tf("sdpa_f32_2x32x8192x128", lambda: nt.scaled_dot_product_attention(qf, kf, vf), fl / 4,
+       cpu=(lambda: F.scaled_dot_product_attention(qfc, kfc, vfc), "1 of 64 (batch, head) pairs, time x 64", 64.0))
+    del qf, kf, vf, qfc, kfc, vfc
     # conv2d (§8 f3; not a BASELINE config): a ResNet-style 3x3 layer, bf16, N32 C256 56x56 ->
     # K256, pad 1 (the CPU leg times one image and scales by 32)
     xc = torch.randn(32, 256, 56, 56, generator=g, device=dev).to(torch.bfloat16)
