@@ -217,3 +217,55 @@ def test_c3_layer_chain_full_one_sequence_checked():
 def test_tolerances_are_the_spec():
     assert TOL[torch.float32] == (1e-5, 1e-5)
     assert TOL[torch.float16] == (1e-2, 1e-2)
+
+
+# ------------------------------------------------------- the other per-op bench lines --------
+# The non-BASELINE lines of the benchmark's per-op table, at the sizes they are timed on.
+
+
+def test_bench_dropout_2p28_bf16():
+    """2^28 bf16 elements, p = 0.1: bit-exact to the oracle on the first / last 64 Ki and 4 Mi
+    sampled elements (the keep mask is Triton's Philox for the same seed)."""
+    import random
+
+    n = 1 << 28
+    x = torch.randn(n, generator=_gen(20), device=DEV).to(torch.bfloat16)
+    random.seed(77)
+    got = nt.dropout(x, 0.1)
+    random.seed(77)
+    seed = random.randrange(0, 2**31)
+    idx = _sample_idx(n, 21)
+    r = O.philox_rand(seed, idx.cpu().numpy()).double()
+    xs = x[idx].cpu()
+    want = O.round_once(torch.where(r > 0.1, xs.double() / 0.9, torch.zeros((), dtype=torch.float64)), torch.bfloat16)
+    assert torch.equal(got[idx].cpu(), want)
+    kept = (got != 0).sum().item() / n
+    assert abs(kept - 0.9) < 1e-3
+
+
+def test_bench_conv2d_resnet_layer():
+    """32 x 256 x 56 x 56 bf16 through 256 3x3 filters (the implicit GEMM): images 0 and 31
+    against the oracle; the channels-last input (no transposed copy) gives the same bits."""
+    g = _gen(22)
+    x = torch.randn((32, 256, 56, 56), generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn((256, 256, 3, 3), generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    out = nt.conv2d(x, w, None, 1, 1)
+    for n in (0, 31):
+        want = O.conv2d(x[n:n + 1].cpu(), w.cpu(), None, stride=1, padding=1)
+        _rel_close(out[n:n + 1], want, 1e-2, 1e-2)
+    out_cl = nt.conv2d(x.contiguous(memory_format=torch.channels_last), w, None, 1, 1)
+    assert torch.equal(out_cl, out)
+
+
+def test_bench_sdpa_fp32():
+    """fp32 attention 2 x 32 x 8192 x 128 (tensor cores through staged fp16 copies): two
+    (batch, head) slices against the oracle within the reference's fp32 tolerance (1e-2)."""
+    g = _gen(23)
+    shape = (2, 32, 8192, 128)
+    q, k, v = (torch.randn(shape, generator=g, device=DEV) for _ in range(3))
+    for causal in (False, True):
+        out = nt.scaled_dot_product_attention(q, k, v, is_causal=causal)
+        for b, h in ((0, 3), (1, 30)):
+            want = O.scaled_dot_product_attention(q[b:b + 1, h:h + 1].cpu(), k[b:b + 1, h:h + 1].cpu(),
+                                                  v[b:b + 1, h:h + 1].cpu(), None, causal, block=1024)
+            assert_close(out[b:b + 1, h:h + 1], want, tol=(1e-2, 1e-2))
