@@ -573,12 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               sm100::tma_load_3d_pair_hint(a_dst + j * BK * kRowBytes, &tma_a, bar, row0 + j * 64, kb * BK, ba,
                                            pol_a);
           }
-          if (p.b_im2col) {
-            int c, w, h, n;
-            uint16_t ow, oh;
-            conv_coords(p, kb, b, col0, c, w, h, n, ow, oh);
-            sm100::tma_load_im2col_4d_pair(b_dst, &tma_b, bar, c, w, h, n, ow, oh);
-          } else if (!p.b_mn) {
+          if (!p.b_mn) {
             sm100::tma_load_3d_pair_hint(b_dst, &tma_b, bar, kb * BK, col0, bb, pol_b);
           } else {
 #pragma unroll
@@ -858,7 +853,7 @@ int pair_slots(int* slots) {
 
 template <typename T, typename TD, int STAGES, int EPI = kEpiPlain>
 int launch_tc_pair(const NtbTensor* a, const NtbTensor* bm, Params p, const Operand& oa, const Operand& ob,
-                   CUtensorMapDataType tdt, cudaStream_t st, const ConvImplicit* cv = nullptr) {
+                   CUtensorMapDataType tdt, cudaStream_t st) {
   using S = PairSmem<STAGES>;
   constexpr int BK = kRowBytes / 2;
   const int es = 2;
@@ -873,9 +868,7 @@ int launch_tc_pair(const NtbTensor* a, const NtbTensor* bm, Params p, const Oper
   else
     rc = tma::encode_3d(&ta, tdt, a->data, p.M, p.K, BA, oa.s_k * es, (BA > 1 ? oa.bs : oa.s_k * p.K) * es, 64, BK);
   if (rc != NTB_OK) return rc;
-  if (cv != nullptr)
-    rc = encode_conv_b(&tb, tdt, *cv, kPairBN / 2);
-  else if (!p.b_mn)
+  if (!p.b_mn)
     rc = tma::encode_3d(&tb, tdt, bm->data, p.K, p.N, BB, ob.s_outer * es, (BB > 1 ? ob.bs : ob.s_outer * p.N) * es,
                         BK, kPairBN / 2);
   else
@@ -1267,17 +1260,14 @@ int conv_implicit_gemm(const ConvImplicit& cv, cudaStream_t st) {
     const double e128 = 0.68 * (double)t128 / (std::ceil((double)t128 / sms) * sms);
     wide = e256 >= e128;
   }
+  // Single-SM tiles even where the plain GEMM would pair CTAs: one im2col load of 256 pixels per
+  // stage beat two of 128 on CTA pairs (a 32-image ResNet 3x3 layer: 0.119 against 0.128 ms).
   if (cv.dtype == NTB_BF16) {
-    if (wide && use_pair(p))
-      return launch_tc_pair<__nv_bfloat16, __nv_bfloat16, 6>(&a, &unused, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                                                             st, &cv);
     return wide ? launch_tc<__nv_bfloat16, __nv_bfloat16, 256, 4>(&a, &unused, p, oa, ob,
                                                                   CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st, &cv)
                 : launch_tc<__nv_bfloat16, __nv_bfloat16, 128, 6>(&a, &unused, p, oa, ob,
                                                                   CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st, &cv);
   }
-  if (wide && use_pair(p))
-    return launch_tc_pair<__half, __half, 6>(&a, &unused, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st, &cv);
   return wide ? launch_tc<__half, __half, 256, 4>(&a, &unused, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st, &cv)
               : launch_tc<__half, __half, 128, 6>(&a, &unused, p, oa, ob, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st, &cv);
 }

@@ -220,17 +220,6 @@ __device__ __forceinline__ void tma_load_im2col_4d(void* smem_dst, const void* t
       "h"(off_h)
       : "memory");
 }
-// The same for a CTA pair running cta_group::2 MMAs (bytes complete on the leader's barrier).
-__device__ __forceinline__ void tma_load_im2col_4d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr,
-                                                        int c, int w, int h, int n, uint16_t off_w, uint16_t off_h) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar_cluster_addr), "h"(off_w),
-      "h"(off_h)
-      : "memory");
-}
-
 // tma_load_3d_pair with an L2 cache policy (createpolicy): operands a raster keeps reused are
 // loaded evict-last, streamed ones evict-first.
 __device__ __forceinline__ void tma_load_3d_pair_hint(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr,
