@@ -11,9 +11,10 @@
 // tensor already is), and one batched GEMM over all images computes
 //   y[n] (as [K, P*Q]) = Wtap [K, R*S*CB*64] x B_n,   B_n[(r, s, c), (p, q)] = x[n, c, p*sh - ph + r*dh, q*sw - pw + s*dw]
 // where each B tile (64 channels of one filter tap x 256 output pixels, or 128 where that
-// quantises better) is one TMA im2col load: the copy engine walks the output pixels' window origins and fetches 64 channels
-// of the tap-shifted input pixel per row (zeros outside the input) straight into the swizzled
-// shared-memory operand layout.  The input is read from HBM about once; no patch matrix exists.
+// quantises better) is one TMA im2col load: the copy engine walks the output pixels' window
+// origins and fetches 64 channels of the tap-shifted input pixel per row (zeros outside the
+// input) straight into the swizzled shared-memory operand layout.  The input is read from HBM
+// about once; no patch matrix exists.
 //
 // im2col + GEMM (fp32 / fp64, fewer than 64 channels, or geometry outside those limits): the
 // images run in chunks of nb: a gather kernel writes, for each image n of the chunk, the patch
