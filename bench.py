@@ -355,6 +355,26 @@ def per_op_table(dev, peaks, with_cpu=True):
     bw("bitwise_or_i32", lambda: nt.bitwise_or(ia, ib), 3 * n * 4, cpu=(lambda: torch.bitwise_or(iac, ibc),))
     bw("bitwise_not_i32", lambda: nt.bitwise_not(ia), 2 * n * 4, cpu=(lambda: torch.bitwise_not(iac),))
     del ia, ib, iac, ibc
+    # §8 f2, the elementwise members with special logic (not a BASELINE config; C2's 2^28 elements)
+    fa = torch.randn(n, generator=g, device=dev) * 4
+    fb = torch.randn(n, generator=g, device=dev) * 4
+    fac = torch.randn(n, generator=gc) * 4 if with_cpu else None
+    fbc = torch.randn(n, generator=gc) * 4 if with_cpu else None
+    bw("copysign_f32", lambda: nt.copysign(fa, fb), 3 * n * 4, cpu=(lambda: torch.copysign(fac, fbc),))
+    bw("nextafter_f32", lambda: nt.nextafter(fa, fb), 3 * n * 4, cpu=(lambda: torch.nextafter(fac, fbc),))
+    bw("lgamma_f32", lambda: nt.lgamma(fa), 2 * n * 4, cpu=(lambda: torch.lgamma(fac),))
+    bw("frac_f32", lambda: nt.frac(fa), 2 * n * 4, cpu=(lambda: torch.frac(fac),))
+    del fb, fbc
+    hb = fa.to(torch.bfloat16)
+    hbc = fac.to(torch.bfloat16) if with_cpu else None
+    bw("rad2deg_bf16", lambda: nt.rad2deg(hb), 2 * n * 2, cpu=(lambda: torch.rad2deg(hbc),))
+    del fa, fac, hb, hbc
+    la = torch.randint(1, 1 << 15, (n,), generator=g, device=dev, dtype=torch.int32)
+    lb = torch.randint(1, 1 << 15, (n,), generator=g, device=dev, dtype=torch.int32)
+    lac = torch.randint(1, 1 << 15, (n,), generator=gc, dtype=torch.int32) if with_cpu else None
+    lbc = torch.randint(1, 1 << 15, (n,), generator=gc, dtype=torch.int32) if with_cpu else None
+    bw("lcm_i32", lambda: nt.lcm(la, lb), 3 * n * 4, cpu=(lambda: torch.lcm(lac, lbc),))
+    del la, lb, lac, lbc
     c1 = torch.randn(4096, 1, generator=g, device=dev)
     r1 = torch.randn(1, 65536, generator=g, device=dev)
     c1c, r1c = c1.cpu(), r1.cpu()

@@ -9,6 +9,8 @@
 
 #include <math.h>
 
+#include <type_traits>
+
 #include "ntb_common.cuh"
 
 namespace ntb {
@@ -335,20 +337,40 @@ struct NextAfter {
   __device__ float operator()(float a, float b) const { return nextafterf(a, b); }
   __device__ double operator()(double a, double b) const { return nextafter(a, b); }
 };
-// lcm(a, b) = |a / gcd(a, b) * b| (0 when either is 0), gcd by Euclid's algorithm.  The
-// product and its absolute value are taken in the C++-promoted type (int for 8/16-bit inputs)
-// before narrowing, which is how torch's lcm treats a result that overflows the input type.
+// Binary (Stein's) gcd of two non-zero unsigned values: strip the common power of two, then
+// repeatedly subtract the smaller odd value from the larger and strip its factors of two.  Only
+// shifts, compares and subtractions: the integer divisions of Euclid's algorithm cost ~20
+// instructions each on the GPU.
+template <typename U>
+__device__ __forceinline__ int ctz_nonzero(U v) {
+  if constexpr (sizeof(U) == 8) return __ffsll((long long)v) - 1;
+  else return __ffs((int)v) - 1;
+}
+template <typename U>
+__device__ __forceinline__ U gcd_binary(U u, U v) {
+  const int shift = ctz_nonzero<U>(u | v);
+  u >>= ctz_nonzero<U>(u);
+  do {
+    v >>= ctz_nonzero<U>(v);
+    const U lo = u < v ? u : v, hi = u < v ? v : u;
+    u = lo;
+    v = hi - lo;
+  } while (v != U(0));
+  return u << shift;
+}
+
+// lcm(a, b) = |a / gcd(a, b) * b| (0 when either is 0).  The gcd of the magnitudes is taken in
+// the unsigned type of the C++-promoted type (int for 8/16-bit inputs); the quotient, product
+// and absolute value in the promoted type before narrowing, which is how torch's lcm treats a
+// result that overflows the input type.
 struct Lcm {
   template <typename T> __device__ T operator()(T a, T b) const {
     using P = decltype(+a);
+    using U = typename std::make_unsigned<P>::type;
     if (a == T(0) || b == T(0)) return T(0);
-    P x = a < T(0) ? -P(a) : P(a), y = b < T(0) ? -P(b) : P(b);
-    while (y != P(0)) {
-      const P t = x % y;
-      x = y;
-      y = t;
-    }
-    P r = P(a) / x * P(b);
+    const U x = a < T(0) ? U(0) - U(P(a)) : U(P(a)), y = b < T(0) ? U(0) - U(P(b)) : U(P(b));
+    const P g = P(gcd_binary<U>(x, y));
+    P r = P(a) / g * P(b);
     return T(r < P(0) ? -r : r);
   }
 };

@@ -41,6 +41,24 @@ def test_lcm_exact(dtype):
     assert torch.equal(nt.lcm(a.to(DEV), b.to(DEV)).cpu(), O.lcm(a, b))
 
 
+@pytest.mark.parametrize("dtype", [torch.int32, torch.int64])
+def test_lcm_wide_values(dtype):
+    # magnitudes up to 2^15 / 2^31, shared powers of two, equal operands, +-1 and the type's
+    # extremes (whose products wrap as the promoted type's arithmetic does)
+    g = torch.Generator().manual_seed(5)
+    hi = 1 << 15 if dtype == torch.int32 else 1 << 31
+    a = torch.randint(-hi, hi, (20000,), generator=g, dtype=dtype)
+    b = torch.randint(-hi, hi, (20000,), generator=g, dtype=dtype)
+    b[::5] = a[::5] * 6
+    b[1::5] = a[1::5]
+    a[2::7] = 1
+    b[3::7] = -1
+    info = torch.iinfo(dtype)
+    a[:4] = torch.tensor([info.max, info.min, info.min, 1 << 20], dtype=dtype)
+    b[:4] = torch.tensor([info.max, 2, info.min, 3 << 12], dtype=dtype)
+    assert torch.equal(nt.lcm(a.to(DEV), b.to(DEV)).cpu(), O.lcm(a, b))
+
+
 @pytest.mark.parametrize("case", CASES, ids=case_id)
 def test_rad2deg_frac_lgamma(case):
     shape, dtype = case
