@@ -631,6 +631,10 @@ def run_case(name, reps):
         xc = torch.randn((32, 256, 56, 56), device=dev, generator=g).to(torch.bfloat16)
         wc = (torch.randn((256, 256, 3, 3), device=dev, generator=g) * 0.02).to(torch.bfloat16)
         fn = lambda: nt.conv2d(xc, wc, None, 1, 1)  # noqa: E731
+    elif name == "sdpa_f32":  # the per-op table's fp32 attention line (staged to fp16)
+        g = torch.Generator(device=dev).manual_seed(0)
+        qf, kf, vf = (torch.randn((2, 32, 8192, 128), device=dev, generator=g) for _ in range(3))
+        fn = lambda: nt.scaled_dot_product_attention(qf, kf, vf)  # noqa: E731
     elif name == "dropout":  # the per-op table's dropout line: p = 0.1 over 2^28 bf16 elements
         g = torch.Generator(device=dev).manual_seed(0)
         xdp = torch.randn(1 << 28, device=dev, generator=g).to(torch.bfloat16)

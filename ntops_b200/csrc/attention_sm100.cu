@@ -693,22 +693,80 @@ struct StageT {
   int64_t sb, sh, ss, sd;   // source strides in elements
   int H, S, D;
   int64_t rows;             // B * H * S
+  int vec;                  // rows load as 16-byte vectors (unit d stride, D and strides multiples
+                            // of 4, 16-byte aligned base)
 };
 struct StageSet {
   StageT t[3];  // Q, K, V (blockIdx.y)
 };
 
-// max |x| of each tensor as float bits (non-negative floats order like their bit patterns);
-// one warp per row, rows grid-strided.
+// Both staging kernels walk chunks of 16 consecutive rows (s) of one (batch, head), one chunk per
+// warp at a time, so the (b, h, s) decomposition is done once per chunk.  With 16-byte loads a
+// row of D floats spans D / 4 lanes and a warp covers 32 / (D / 4) rows per step; four steps'
+// loads are issued before any is used.
+constexpr int kStageChunk = 16;
+
+template <bool VEC>
+__device__ __forceinline__ void stage_rows(const StageT& a, int64_t chunk, float& m, int e, bool write) {
+  const int64_t cps = (a.S + kStageChunk - 1) / kStageChunk;
+  const int64_t bh = chunk / cps;
+  const int s0 = (int)(chunk - bh * cps) * kStageChunk;
+  const int64_t b = bh / a.H, h = bh - b * a.H;
+  const float* base = a.src + b * a.sb + h * a.sh;
+  __half* dbase = a.dst + bh * (int64_t)a.S * a.D;
+  const int lane = threadIdx.x & 31;
+  if constexpr (VEC) {
+    const int lpr = a.D >> 2, rpw = 32 / lpr;
+    const int sub = lane / lpr, c4 = (lane - sub * lpr) * 4;
+#pragma unroll 1
+    for (int k = 0; k < kStageChunk; k += 4 * rpw) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int si = s0 + k + u * rpw + sub;
+        v[u] = (k + u * rpw + sub < kStageChunk && si < a.S)
+                   ? *reinterpret_cast<const float4*>(base + (int64_t)si * a.ss + c4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int si = s0 + k + u * rpw + sub;
+        if (!write) {
+          m = fmaxf(m, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+        } else if (k + u * rpw + sub < kStageChunk && si < a.S) {
+          __half2 lo = __floats2half2_rn(ldexpf(v[u].x, e), ldexpf(v[u].y, e));
+          __half2 hi = __floats2half2_rn(ldexpf(v[u].z, e), ldexpf(v[u].w, e));
+          uint2 w;
+          w.x = *reinterpret_cast<uint32_t*>(&lo);
+          w.y = *reinterpret_cast<uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(dbase + (int64_t)si * a.D + c4) = w;
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int k = 0; k < kStageChunk; ++k) {
+      const int si = s0 + k;
+      if (si >= a.S) break;
+      const float* x = base + (int64_t)si * a.ss;
+      for (int d = lane; d < a.D; d += 32) {
+        const float xv = x[(int64_t)d * a.sd];
+        if (!write) m = fmaxf(m, fabsf(xv));
+        else dbase[(int64_t)si * a.D + d] = __float2half_rn(ldexpf(xv, e));
+      }
+    }
+  }
+}
+
+// max |x| of each tensor as float bits (non-negative floats order like their bit patterns).
 __global__ void __launch_bounds__(256) stage_max_kernel(StageSet set, unsigned int* maxbits) {
   const StageT& a = set.t[blockIdx.y];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t chunks = (a.rows / a.S) * ((a.S + kStageChunk - 1) / kStageChunk);
   float m = 0.f;
-  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.rows; row += (int64_t)gridDim.x * 8) {
-    const int64_t bh = row / a.S, si = row - bh * a.S;
-    const int64_t b = bh / a.H, h = bh - b * a.H;
-    const float* x = a.src + b * a.sb + h * a.sh + si * a.ss;
-    for (int d = lane; d < a.D; d += 32) m = fmaxf(m, fabsf(x[d * a.sd]));
+  for (int64_t c = (int64_t)blockIdx.x * 8 + warp; c < chunks; c += (int64_t)gridDim.x * 8) {
+    if (a.vec) stage_rows<true>(a, c, m, 0, false);
+    else stage_rows<false>(a, c, m, 0, false);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -718,13 +776,12 @@ __global__ void __launch_bounds__(256) stage_max_kernel(StageSet set, unsigned i
 __global__ void __launch_bounds__(256) stage_convert_kernel(StageSet set, const unsigned int* maxbits) {
   const StageT& a = set.t[blockIdx.y];
   const int e = stage_exp(maxbits[blockIdx.y]);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.rows; row += (int64_t)gridDim.x * 8) {
-    const int64_t bh = row / a.S, si = row - bh * a.S;
-    const int64_t b = bh / a.H, h = bh - b * a.H;
-    const float* x = a.src + b * a.sb + h * a.sh + si * a.ss;
-    __half* y = a.dst + row * a.D;
-    for (int d = lane; d < a.D; d += 32) y[d] = __float2half_rn(ldexpf(x[d * a.sd], e));
+  const int warp = threadIdx.x >> 5;
+  const int64_t chunks = (a.rows / a.S) * ((a.S + kStageChunk - 1) / kStageChunk);
+  float unused = 0.f;
+  for (int64_t c = (int64_t)blockIdx.x * 8 + warp; c < chunks; c += (int64_t)gridDim.x * 8) {
+    if (a.vec) stage_rows<true>(a, c, unused, e, true);
+    else stage_rows<false>(a, c, unused, e, true);
   }
 }
 
@@ -993,7 +1050,12 @@ int sdpa_impl(const NtbTensor* q, const NtbTensor* k, const NtbTensor* v, const 
       a.S = (int)t->shape[2];
       a.D = (int)t->shape[3];
       a.rows = t->shape[0] * t->shape[1] * t->shape[2];
-      if (a.rows > max_rows) max_rows = a.rows;
+      a.vec = a.sd == 1 && a.D % 4 == 0 && a.D <= 128 && 32 % (a.D / 4) == 0 &&
+              reinterpret_cast<uintptr_t>(a.src) % 16 == 0 &&
+              (a.ss % 4 == 0 || t->shape[2] == 1) && (a.sh % 4 == 0 || t->shape[1] == 1) &&
+              (a.sb % 4 == 0 || t->shape[0] == 1);
+      const int64_t chunks = (a.rows / a.S) * ((a.S + kStageChunk - 1) / kStageChunk);
+      if (chunks > max_rows) max_rows = chunks;
       cur += (t->shape[0] * t->shape[1] * t->shape[2] * t->shape[3] * 2 + 255) / 256 * 256;
     }
     NTB_CUDA(cudaMemsetAsync(maxbits, 0, 3 * sizeof(unsigned int), st));

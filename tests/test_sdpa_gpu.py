@@ -200,6 +200,7 @@ FP32_TC_CASES = [
     (1, 4, 4, 777, 777, 128, 1e-3, CausalVariant.UPPER_LEFT, "bhsd"),
     (2, 4, 1, 200, 640, 64, 37.0, CausalVariant.LOWER_RIGHT, "bshd"),
     (1, 2, 2, 2048, 2048, 128, 0.05, CausalVariant.UPPER_LEFT, "bshd"),
+    (2, 4, 2, 333, 400, 64, 3.0, None, "offset"),  # rows not 16-byte aligned: element-wise staging
 ]
 
 
@@ -213,6 +214,8 @@ def test_fp32_tensor_core_staged(case):
     scale = 1.0 / (math.sqrt(d) * mag * mag) if mag != 1.0 else None
     if layout == "bshd":
         qd, kd, vd = (t.transpose(1, 2).contiguous().to(DEV).transpose(1, 2) for t in (q, k, v))
+    elif layout == "offset":  # views one element into wider rows
+        qd, kd, vd = (torch.cat((torch.zeros(t.shape[:-1] + (1,)), t), -1).to(DEV)[..., 1:] for t in (q, k, v))
     else:
         qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
     kw = {}
