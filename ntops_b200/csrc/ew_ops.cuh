@@ -113,10 +113,6 @@ struct Rad2Deg {
 struct Frac {
   template <typename T> __device__ T operator()(T x) const { return x - m_trunc(x); }
 };
-struct Lgamma {
-  __device__ float operator()(float x) const { return lgammaf(x); }
-  __device__ double operator()(double x) const { return lgamma(x); }
-};
 
 // ------------------------------------------------- fast forms for 16-bit outputs ----------
 // Used only when the result is rounded to fp16 / bf16: the hardware approximations below
@@ -132,6 +128,50 @@ __device__ __forceinline__ float hw_lg2(float x) {
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// log |Gamma(x)| in fp32 from published formulas (CUDA's lgammaf is a long, branchy routine):
+//  * z >= 4: Stirling's asymptotic series (Abramowitz & Stegun 6.1.40),
+//      lgamma(z) = (z - 1/2) ln z - z + ln(2 pi) / 2 + 1/(12 z) - 1/(360 z^3) + 1/(1260 z^5)
+//                  - 1/(1680 z^7) + 1/(1188 z^9),
+//    whose truncation error is below 691 / (360360 z^11) < 5e-10;
+//  * 0 < t < 4: the recurrence Gamma(t + 1) = t Gamma(t) (A&S 6.1.15) carries t up to
+//    z = t + n in [4, 5): lgamma(t) = lgamma(z) - ln(t (t + 1) ... (t + n - 1));
+//  * x <= 0: the reflection formula Gamma(x) Gamma(1 - x) = pi / sin(pi x) (A&S 6.1.17),
+//    lgamma(x) = ln pi - ln |sin(pi x)| - lgamma(1 - x), with sin(pi x) from sinpif;
+//  * the poles (0 and the negative integers) and +-inf give +inf; NaN stays NaN.
+// The logarithms come from the hardware base-2 logarithm (absolute error ~2^-22 in log2), logf
+// only for subnormal products.  Absolute error ~1e-6 where the terms cancel (near the zeros at 1
+// and 2, and of the reflected branch), ~1e-7 relative elsewhere.
+struct Lgamma {
+  __device__ float operator()(float x) const {
+    if (isnan(x)) return x;
+    if (isinf(x)) return INFINITY;
+    const bool neg = x <= 0.f;
+    const float t = neg ? 1.f - x : x;
+    float prod = 1.f, z = t;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const bool step = z < 4.f;
+      prod = step ? prod * z : prod;
+      z = step ? z + 1.f : z;
+    }
+    const float r = __frcp_rn(z), r2 = r * r;
+    float poly = fmaf(r2, 1.f / 1188.f, -1.f / 1680.f);
+    poly = fmaf(r2, poly, 1.f / 1260.f);
+    poly = fmaf(r2, poly, -1.f / 360.f);
+    poly = fmaf(r2, poly, 1.f / 12.f);
+    const float lz = hw_lg2(z) * 0.69314718055994530942f;
+    float res = fmaf(z - 0.5f, lz, -z) + fmaf(r, poly, 0.91893853320467274178f);
+    // the hardware logarithm flushes subnormal inputs: logf for products below 2^-100
+    if (prod != 1.f) res -= prod < 7.8886091e-31f ? logf(prod) : hw_lg2(prod) * 0.69314718055994530942f;
+    if (neg) {
+      const float sn = fabsf(sinpif(x));  // >= ~3e-7 unless x is an integer (fp32 spacing)
+      res = sn == 0.f ? INFINITY : 1.14472988584940017414f - hw_lg2(sn) * 0.69314718055994530942f - res;
+    }
+    return res;
+  }
+  __device__ double operator()(double x) const { return lgamma(x); }
+};
 __device__ __forceinline__ float hw_rcp(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -72,6 +72,25 @@ def test_rad2deg_frac_lgamma(case):
     assert_close(got, want, tol=tol)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_lgamma_wide_range(dtype):
+    # negative non-integers (reflection), points next to the poles and to the zeros at 1 and 2,
+    # tiny and huge magnitudes, and the special values
+    g = torch.Generator().manual_seed(8)
+    parts = [torch.randn(20000, generator=g) * 6,
+             torch.exp2(torch.rand(5000, generator=g) * 200 - 100),
+             torch.exp2(torch.rand(5000, generator=g) * 120),
+             -torch.arange(1, 40).float() + torch.tensor(1e-3).expand(39),
+             -torch.arange(1, 40).float() - torch.tensor(1e-3).expand(39),
+             1 + torch.linspace(-1e-3, 1e-3, 101), 2 + torch.linspace(-1e-3, 1e-3, 101),
+             torch.tensor([0.0, -0.0, -1.0, -7.0, 1.0, 2.0, float("inf"), float("-inf"), float("nan"), 1e-38, 3e36])]
+    x = torch.cat(parts).to(dtype)
+    got = nt.lgamma(x.to(DEV)).cpu()
+    want = O.lgamma(x)
+    tol = (1e-5, 1e-5) if dtype == torch.float32 else None
+    assert_close(got, want, tol=tol, equal_nan=True)
+
+
 def test_rad2deg_int_promotes():
     i = torch.arange(-10, 10, dtype=torch.int32)
     assert_close(nt.rad2deg(i.to(DEV)), O.rad2deg(i))
