@@ -229,6 +229,7 @@ struct PowFast {
   // capped at 80 registers (3 blocks per SM): the extra warps hide the MUFU latency (bf16
   // 0.56 -> 0.64 of HBM, fp16 0.72 -> 0.73)
   static constexpr int kMinBlocks = 3;
+  static constexpr bool kUnpackPairs = true;  // bf16 inputs widened from their 32-bit words
   __device__ float operator()(float a, float b) const { return pow_rules(a, b, hw_ex2(b * hw_lg2(fabsf(a)))); }
 };
 
